@@ -1,0 +1,110 @@
+/*
+ * tattn_b200 -- C ABI of the B200-native FlashAttention-2 forward/backward.
+ *
+ * This is the drop-in boundary for the reference's kernel layer (amaanmithani/triton-attn,
+ * src/tattn/kernels.py): each entry point replaces one Triton kernel launch made by the reference's
+ * host glue (src/tattn/api.py). Plain pointers and sizes only; any host language binds it through
+ * its FFI (the Python package `tattn` uses ctypes).
+ *
+ * Conventions shared by every entry point
+ *   - Tensors are logically [Z, H, N, D] (batch, heads, sequence, head dim) and are given by a device
+ *     pointer plus four element strides in (z, h, n, d) order, exactly like the reference kernels'
+ *     (stride_*z, stride_*h, stride_*m|n, stride_*d) arguments (kernels.py:63-88, 157-179, 248-269).
+ *   - dtype: TATTN_F16 (IEEE half; runs on the tcgen05 tensor cores) or TATTN_F32 (runs exact fp32
+ *     CUDA-core kernels). D must be 16, 32, 64 or 128 (api.py:53).
+ *   - M and delta are dense fp32 [Z, H, N] (index (z*H + h)*N + n), as kernels.py:143 / 193-194.
+ *     M = rowmax + log2(rowsum) of the base-2 scaled scores S*sm_scale*log2(e).
+ *   - Gradients dq, dk, dv are written dense and contiguous [Z, H, N, D] (api.py:111-113).
+ *   - The causal mask keeps row >= col (top-left aligned, equal query and key length).
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream). Calls are asynchronous; they only
+ *     enqueue work. The caller allocates every buffer; the library allocates no device memory.
+ *   - fp16 tensors read through TMA need: unit D stride, 16-byte aligned base, and (z, h, n) strides
+ *     that are multiples of 8 elements (strides of extent-1 dimensions are ignored). Otherwise the
+ *     call returns TATTN_ERR_LAYOUT and the caller makes the tensor contiguous (and aligned).
+ *   - Return value: TATTN_OK or one of the TATTN_ERR_* codes below; nothing is launched on error.
+ *   - Kernel-side failures (a bounded wait that ran out) are recorded in a per-device status word,
+ *     read with tattn_device_status().
+ */
+#ifndef TATTN_B200_H_
+#define TATTN_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TATTN_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define TATTN_API __attribute__((visibility("default")))
+#else
+#define TATTN_API
+#endif
+
+enum tattn_dtype { TATTN_F16 = 0, TATTN_F32 = 1 };
+
+enum tattn_status {
+  TATTN_OK = 0,
+  TATTN_ERR_INVALID_ARGUMENT = 1, /* bad dims, dtype, head dim, null pointer */
+  TATTN_ERR_LAYOUT = 2,           /* strides/alignment not addressable by TMA: make contiguous */
+  TATTN_ERR_CUDA = 3,             /* a CUDA runtime/driver call or a launch failed */
+  TATTN_ERR_NO_DEVICE = 4,        /* current device is not sm_100 or the TMA encoder is missing */
+  TATTN_ERR_DEVICE_STATUS = 5,    /* a kernel recorded a failure in the device status word */
+  TATTN_ERR_UNSUPPORTED = 6       /* valid request this build does not implement */
+};
+
+/* Device status word bits (tattn_device_status). */
+#define TATTN_DEV_WAIT_TIMEOUT 1 /* an mbarrier wait exceeded its 1 s limit; the CTA unwound */
+#define TATTN_DEV_ABORTED 2
+
+/* Forward: O = softmax(Q K^T * sm_scale) V and M, for one attention call.
+ * Replaces the launch of _fwd_kernel (src/tattn/kernels.py:57-148) made by _forward
+ * (src/tattn/api.py:78-99). strides: 16 int64 = q, k, v, o each (z, h, n, d).
+ * tile_cfg: 0 = the tuned default; other values select tile variants (tattn_tile_configs). */
+TATTN_API int tattn_fwd(const void* q, const void* k, const void* v, void* o, float* m, const int64_t* strides, int Z,
+              int H, int N, int D, int dtype, int causal, float sm_scale, int tile_cfg, void* stream);
+
+/* Backward preprocess: delta = rowsum(dO * O) in fp32.
+ * Replaces _bwd_preprocess (src/tattn/kernels.py:324-337), launched at api.py:122.
+ * strides: 8 int64 = o, dout each (z, h, n, d); both need a unit D stride and 16-byte aligned rows. */
+TATTN_API int tattn_bwd_preprocess(const void* o, const void* dout, float* delta, const int64_t* strides, int Z, int H,
+                         int N, int D, int dtype, void* stream);
+
+/* Backward dK/dV, one CTA per key block, no atomics: dV = P^T dO, dK = dS^T Q * sm_scale.
+ * Replaces _bwd_dkdv_kernel (src/tattn/kernels.py:151-239), launched at api.py:124-142.
+ * strides: 16 int64 = q, k, v, dout each (z, h, n, d). dk, dv: dense [Z, H, N, D]. */
+TATTN_API int tattn_bwd_dkdv(const void* q, const void* k, const void* v, const void* dout, void* dk, void* dv,
+                   const float* m, const float* delta, const int64_t* strides, int Z, int H, int N, int D,
+                   int dtype, int causal, float sm_scale, int tile_cfg, void* stream);
+
+/* Backward dQ, one CTA per query block: dQ = dS K * sm_scale.
+ * Replaces _bwd_dq_kernel (src/tattn/kernels.py:242-321), launched at api.py:143-145.
+ * strides: 16 int64 = q, k, v, dout each (z, h, n, d). dq: dense [Z, H, N, D]. */
+TATTN_API int tattn_bwd_dq(const void* q, const void* k, const void* v, const void* dout, void* dq, const float* m,
+                 const float* delta, const int64_t* strides, int Z, int H, int N, int D, int dtype, int causal,
+                 float sm_scale, int tile_cfg, void* stream);
+
+/* Can the fp16 tensor-core path read this tensor in place? Returns 1 (yes) or 0 (make it contiguous).
+ * strides: 4 int64 (z, h, n, d). Mirrors the check every fp16 entry point applies. */
+TATTN_API int tattn_layout_ok(const void* ptr, const int64_t* strides, int Z, int H, int N, int D);
+
+/* Number of tile variants per kernel family (valid tile_cfg values are 0 .. n-1); kind: 0 = forward,
+ * 1 = backward. Stands in for the reference's autotune spaces (kernels.py:21-41); 0 is the default. */
+TATTN_API int tattn_tile_configs(int kind);
+
+/* Synchronise `stream`, then report the current device's status word (TATTN_DEV_* bits) in *out and
+ * clear it when `clear` is nonzero. Returns TATTN_OK, or TATTN_ERR_CUDA if the sync failed. */
+TATTN_API int tattn_device_status(void* stream, int* out, int clear);
+
+/* Static description of a status code. */
+TATTN_API const char* tattn_status_string(int status);
+
+/* TATTN_ABI_VERSION of the loaded library. */
+TATTN_API int tattn_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TATTN_B200_H_ */

@@ -1,0 +1,305 @@
+// C-ABI boundary (include/tattn.h): argument validation, TMA tensor-map encoding, dispatch to the
+// kernel launchers, and the per-device status word that kernels write when a bounded wait runs out.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <mutex>
+
+#include "../../include/tattn.h"
+#include "kernels.h"
+
+namespace tattn {
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Kernel-side failure bits (tattn_device_status). One word per device, in the module's own global
+// memory; kernels get its address as a plain pointer.
+__device__ int g_status_word;
+
+struct DeviceState {
+  bool init = false;
+  int err = TATTN_OK;
+  int* status = nullptr;
+};
+
+std::mutex g_mu;
+DeviceState g_dev[kMaxDevices];
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int current_device(int* dev) {
+  if (cudaGetDevice(dev) != cudaSuccess) return TATTN_ERR_CUDA;
+  if (*dev < 0 || *dev >= kMaxDevices) return TATTN_ERR_NO_DEVICE;
+  return TATTN_OK;
+}
+
+// Once per device (with that device current): check it is sm_100 and resolve the status word address.
+int device_setup(DeviceState** out) {
+  int dev;
+  int rc = current_device(&dev);
+  if (rc != TATTN_OK) return rc;
+  std::lock_guard<std::mutex> lock(g_mu);
+  DeviceState& st = g_dev[dev];
+  if (!st.init) {
+    st.init = true;
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) {
+      st.err = TATTN_ERR_CUDA;
+    } else if (prop.major != 10) {
+      st.err = TATTN_ERR_NO_DEVICE;
+    } else if (cudaGetSymbolAddress(reinterpret_cast<void**>(&st.status), g_status_word) != cudaSuccess) {
+      st.err = TATTN_ERR_CUDA;
+    } else if (g_encode == nullptr) {
+      cudaDriverEntryPointQueryResult q;
+      void* fn = nullptr;
+      if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+          q != cudaDriverEntryPointSuccess || fn == nullptr) {
+        st.err = TATTN_ERR_NO_DEVICE;
+      } else {
+        g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+      }
+    }
+  }
+  *out = &st;
+  return st.err;
+}
+
+bool valid_dims(int Z, int H, int N, int D) {
+  return Z >= 0 && H >= 0 && N >= 0 && (D == 16 || D == 32 || D == 64 || D == 128);
+}
+
+Strides4 load_strides(const int64_t* s) { return Strides4{s[0], s[1], s[2], s[3]}; }
+
+// Strides of extent-1 dimensions never move an address; replace them by the dense value so the TMA
+// stride rules only see strides that matter.
+Strides4 normalize(Strides4 s, int Z, int H, int N, int D) {
+  if (N <= 1) s.n = D;
+  if (H <= 1) s.h = int64_t(N) * s.n;
+  if (Z <= 1) s.z = int64_t(H) * s.h;
+  return s;
+}
+
+bool layout_ok(const void* p, Strides4 s, int Z, int H, int N, int D) {
+  s = normalize(s, Z, H, N, D);
+  if (s.d != 1) return false;
+  if ((reinterpret_cast<uintptr_t>(p) & 15u) != 0) return false;
+  const int64_t lim = int64_t(1) << 38;
+  for (int64_t x : {s.n, s.h, s.z}) {
+    if (x <= 0 || x % 8 != 0 || x >= lim) return false;
+  }
+  return true;
+}
+
+// [Z, H, N, D] fp16 tensor as a 4-D TMA map {D, N, H, Z}; box = {min(D, 64) columns, box_rows rows}
+// with the swizzle that matches one row chunk (32/64/128 bytes).
+int encode_f16(CUtensorMap* tm, const void* p, Strides4 s, int Z, int H, int N, int D, int box_rows) {
+  s = normalize(s, Z, H, N, D);
+  const int cw = D < 64 ? D : 64;
+  cuuint64_t dims[4] = {cuuint64_t(D), cuuint64_t(N), cuuint64_t(H), cuuint64_t(Z)};
+  cuuint64_t strides[3] = {cuuint64_t(s.n) * 2, cuuint64_t(s.h) * 2, cuuint64_t(s.z) * 2};
+  cuuint32_t box[4] = {cuuint32_t(cw), cuuint32_t(box_rows), 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapSwizzle sw = cw == 64 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                         : (cw == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+  CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(p), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? TATTN_OK : TATTN_ERR_LAYOUT;
+}
+
+int cuda_rc(cudaError_t e) {
+  if (e == cudaSuccess) return TATTN_OK;
+  if (e == cudaErrorNotSupported) return TATTN_ERR_UNSUPPORTED;
+  return TATTN_ERR_CUDA;
+}
+
+}  // namespace
+}  // namespace tattn
+
+using namespace tattn;
+
+extern "C" int tattn_fwd(const void* q, const void* k, const void* v, void* o, float* m, const int64_t* strides,
+                         int Z, int H, int N, int D, int dtype, int causal, float sm_scale, int tile_cfg,
+                         void* stream) {
+  if (!strides || !valid_dims(Z, H, N, D) || (dtype != TATTN_F16 && dtype != TATTN_F32) || tile_cfg < 0 ||
+      tile_cfg >= tattn_tile_configs(0))
+    return TATTN_ERR_INVALID_ARGUMENT;
+  if (int64_t(Z) * H * N == 0) return TATTN_OK;
+  if (!q || !k || !v || !o || !m) return TATTN_ERR_INVALID_ARGUMENT;
+  DeviceState* st;
+  int rc = device_setup(&st);
+  if (rc != TATTN_OK) return rc;
+  const Strides4 sq = load_strides(strides), sk = load_strides(strides + 4), sv = load_strides(strides + 8),
+                 so = load_strides(strides + 12);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  FwdArgs a{};
+  a.o = o;
+  a.m = m;
+  a.so = so;
+  a.Z = Z;
+  a.H = H;
+  a.N = N;
+  a.status = st->status;
+  if (dtype == TATTN_F32) {
+    a.qk_scale = sm_scale * kLog2e;
+    return cuda_rc(launch_fwd_f32(D, causal != 0, q, k, v, sq, sk, sv, a, sm_scale, s));
+  }
+  if (!layout_ok(q, sq, Z, H, N, D) || !layout_ok(k, sk, Z, H, N, D) || !layout_ok(v, sv, Z, H, N, D) ||
+      !layout_ok(o, so, Z, H, N, D))
+    return TATTN_ERR_LAYOUT;
+  a.so = normalize(so, Z, H, N, D);
+  a.qk_scale = (sm_scale < 0.f ? -sm_scale : sm_scale) * kLog2e;
+  a.negate_s = sm_scale < 0.f ? 1 : 0;
+  CUtensorMap tq, tk, tv;
+  if ((rc = encode_f16(&tq, q, sq, Z, H, N, D, 128)) != TATTN_OK) return rc;
+  if ((rc = encode_f16(&tk, k, sk, Z, H, N, D, 128)) != TATTN_OK) return rc;
+  if ((rc = encode_f16(&tv, v, sv, Z, H, N, D, 128)) != TATTN_OK) return rc;
+  return cuda_rc(launch_fwd_f16(D, causal != 0, tile_cfg, tq, tk, tv, a, s));
+}
+
+extern "C" int tattn_bwd_preprocess(const void* o, const void* dout, float* delta, const int64_t* strides, int Z,
+                                    int H, int N, int D, int dtype, void* stream) {
+  if (!strides || !valid_dims(Z, H, N, D) || (dtype != TATTN_F16 && dtype != TATTN_F32))
+    return TATTN_ERR_INVALID_ARGUMENT;
+  if (int64_t(Z) * H * N == 0) return TATTN_OK;
+  if (!o || !dout || !delta) return TATTN_ERR_INVALID_ARGUMENT;
+  DeviceState* st;
+  int rc = device_setup(&st);
+  if (rc != TATTN_OK) return rc;
+  BwdArgs a{};
+  a.o = o;
+  a.dout = dout;
+  a.so = load_strides(strides);
+  a.sdo = load_strides(strides + 4);
+  // Rows are read with 16-byte vector loads: same rules as the TMA path (fp32 rows are 16-byte
+  // aligned whenever fp16-style strides hold with half the element count, checked here directly).
+  const int esz = dtype == TATTN_F16 ? 2 : 4;
+  for (const auto& pr : {std::make_pair(o, a.so), std::make_pair(dout, a.sdo)}) {
+    Strides4 s = normalize(pr.second, Z, H, N, D);
+    if (s.d != 1 || (reinterpret_cast<uintptr_t>(pr.first) & 15u) != 0) return TATTN_ERR_LAYOUT;
+    for (int64_t x : {s.n, s.h, s.z})
+      if ((x * esz) % 16 != 0) return TATTN_ERR_LAYOUT;
+  }
+  a.so = normalize(a.so, Z, H, N, D);
+  a.sdo = normalize(a.sdo, Z, H, N, D);
+  a.delta = delta;
+  a.Z = Z;
+  a.H = H;
+  a.N = N;
+  a.status = st->status;
+  return cuda_rc(launch_bwd_preprocess(D, dtype == TATTN_F16, a, static_cast<cudaStream_t>(stream)));
+}
+
+namespace {
+
+int bwd_common(bool dq_pass, const void* q, const void* k, const void* v, const void* dout, void* dq, void* dk,
+               void* dv, const float* m, const float* delta, const int64_t* strides, int Z, int H, int N, int D,
+               int dtype, int causal, float sm_scale, int tile_cfg, void* stream) {
+  if (!strides || !valid_dims(Z, H, N, D) || (dtype != TATTN_F16 && dtype != TATTN_F32) || tile_cfg < 0 ||
+      tile_cfg >= tattn_tile_configs(1))
+    return TATTN_ERR_INVALID_ARGUMENT;
+  if (int64_t(Z) * H * N == 0) return TATTN_OK;
+  if (!q || !k || !v || !dout || !m || !delta) return TATTN_ERR_INVALID_ARGUMENT;
+  if (dq_pass ? !dq : (!dk || !dv)) return TATTN_ERR_INVALID_ARGUMENT;
+  DeviceState* st;
+  int rc = device_setup(&st);
+  if (rc != TATTN_OK) return rc;
+  BwdArgs a{};
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.dout = dout;
+  a.sq = load_strides(strides);
+  a.sk = load_strides(strides + 4);
+  a.sv = load_strides(strides + 8);
+  a.sdo = load_strides(strides + 12);
+  a.m = m;
+  a.delta = const_cast<float*>(delta);
+  a.dq = dq;
+  a.dk = dk;
+  a.dv = dv;
+  a.Z = Z;
+  a.H = H;
+  a.N = N;
+  a.sm_scale = sm_scale;
+  a.qk_scale = (sm_scale < 0.f ? -sm_scale : sm_scale) * kLog2e;
+  a.negate_s = sm_scale < 0.f ? 1 : 0;
+  a.status = st->status;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == TATTN_F32)
+    return cuda_rc(dq_pass ? launch_bwd_dq_f32(D, causal != 0, a, s) : launch_bwd_dkdv_f32(D, causal != 0, a, s));
+  if (!layout_ok(q, a.sq, Z, H, N, D) || !layout_ok(k, a.sk, Z, H, N, D) || !layout_ok(v, a.sv, Z, H, N, D) ||
+      !layout_ok(dout, a.sdo, Z, H, N, D))
+    return TATTN_ERR_LAYOUT;
+  const int64_t dense_n = D;
+  if ((reinterpret_cast<uintptr_t>(dq_pass ? dq : dk) & 15u) != 0 || (!dq_pass && (reinterpret_cast<uintptr_t>(dv) & 15u)))
+    return TATTN_ERR_LAYOUT;
+  (void)dense_n;
+  CUtensorMap tq, tk, tv, tdo;
+  // dQ: query tiles of 128 rows, key blocks of 64 rows; dK/dV: key tiles of 128 rows, query blocks of 64.
+  const int q_rows = dq_pass ? 128 : 64, kv_rows = dq_pass ? 64 : 128;
+  if ((rc = encode_f16(&tq, q, a.sq, Z, H, N, D, q_rows)) != TATTN_OK) return rc;
+  if ((rc = encode_f16(&tk, k, a.sk, Z, H, N, D, kv_rows)) != TATTN_OK) return rc;
+  if ((rc = encode_f16(&tv, v, a.sv, Z, H, N, D, kv_rows)) != TATTN_OK) return rc;
+  if ((rc = encode_f16(&tdo, dout, a.sdo, Z, H, N, D, q_rows)) != TATTN_OK) return rc;
+  return cuda_rc(dq_pass ? launch_bwd_dq_f16(D, causal != 0, tile_cfg, tq, tk, tv, tdo, a, s)
+                         : launch_bwd_dkdv_f16(D, causal != 0, tile_cfg, tq, tk, tv, tdo, a, s));
+}
+
+}  // namespace
+
+extern "C" int tattn_bwd_dkdv(const void* q, const void* k, const void* v, const void* dout, void* dk, void* dv,
+                              const float* m, const float* delta, const int64_t* strides, int Z, int H, int N,
+                              int D, int dtype, int causal, float sm_scale, int tile_cfg, void* stream) {
+  return bwd_common(false, q, k, v, dout, nullptr, dk, dv, m, delta, strides, Z, H, N, D, dtype, causal, sm_scale,
+                    tile_cfg, stream);
+}
+
+extern "C" int tattn_bwd_dq(const void* q, const void* k, const void* v, const void* dout, void* dq,
+                            const float* m, const float* delta, const int64_t* strides, int Z, int H, int N, int D,
+                            int dtype, int causal, float sm_scale, int tile_cfg, void* stream) {
+  return bwd_common(true, q, k, v, dout, dq, nullptr, nullptr, m, delta, strides, Z, H, N, D, dtype, causal,
+                    sm_scale, tile_cfg, stream);
+}
+
+extern "C" int tattn_layout_ok(const void* ptr, const int64_t* strides, int Z, int H, int N, int D) {
+  if (!strides || !valid_dims(Z, H, N, D)) return 0;
+  return layout_ok(ptr, load_strides(strides), Z, H, N, D) ? 1 : 0;
+}
+
+extern "C" int tattn_tile_configs(int kind) { return kind == 0 || kind == 1 ? 1 : 0; }
+
+extern "C" int tattn_device_status(void* stream, int* out, int clear) {
+  if (!out) return TATTN_ERR_INVALID_ARGUMENT;
+  DeviceState* st;
+  int rc = device_setup(&st);
+  if (rc != TATTN_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaStreamSynchronize(s) != cudaSuccess) return TATTN_ERR_CUDA;
+  int v = 0;
+  if (cudaMemcpy(&v, st->status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return TATTN_ERR_CUDA;
+  if (clear && v != 0) {
+    const int zero = 0;
+    if (cudaMemcpy(st->status, &zero, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) return TATTN_ERR_CUDA;
+  }
+  *out = v;
+  return TATTN_OK;
+}
+
+extern "C" const char* tattn_status_string(int status) {
+  switch (status) {
+    case TATTN_OK: return "ok";
+    case TATTN_ERR_INVALID_ARGUMENT: return "invalid argument (dims, dtype, head dim or null pointer)";
+    case TATTN_ERR_LAYOUT: return "layout not addressable by TMA (needs unit D stride, 16-byte alignment)";
+    case TATTN_ERR_CUDA: return "CUDA runtime or launch failure";
+    case TATTN_ERR_NO_DEVICE: return "current device is not an sm_100 GPU (or the TMA encoder is unavailable)";
+    case TATTN_ERR_DEVICE_STATUS: return "a kernel recorded a failure in the device status word";
+    case TATTN_ERR_UNSUPPORTED: return "not implemented by this build";
+    default: return "unknown status";
+  }
+}
+
+extern "C" int tattn_abi_version(void) { return TATTN_ABI_VERSION; }

@@ -1,0 +1,58 @@
+// Host-side launcher interface between the C-ABI layer (capi.cu) and the kernel translation units.
+// Nothing here is exported from the shared library; include/tattn.h is the public boundary.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace tattn {
+
+// Element strides of one [Z, H, N, D] tensor (the D stride is always 1 for the fp16 kernels).
+struct Strides4 {
+  int64_t z, h, n, d;
+};
+
+struct FwdArgs {
+  void* o;           // [Z, H, N, D], strides `so`
+  float* m;          // [Z, H, N] dense fp32: rowmax + log2(rowsum), base-2 units
+  Strides4 so;
+  int Z, H, N;
+  float qk_scale;    // |sm_scale| * log2(e); the sign goes into the S MMA (negate A) for fp16
+  int negate_s;      // 1 when sm_scale < 0 (fp16 path)
+  int* status;       // device status word
+};
+
+struct BwdArgs {
+  // inputs
+  const void* q; const void* k; const void* v; const void* o; const void* dout;
+  Strides4 sq, sk, sv, so, sdo;
+  const float* m;    // [Z, H, N]
+  float* delta;      // [Z, H, N]: rowsum(dO * O)
+  // outputs (dense [Z, H, N, D])
+  void* dq; void* dk; void* dv;
+  int Z, H, N;
+  float sm_scale;    // signed
+  float qk_scale;    // |sm_scale| * log2(e)
+  int negate_s;
+  int* status;
+};
+
+// fp16 tcgen05 kernels (tensor maps describe [Z, H, N, D] tensors as 4-D {D, N, H, Z}).
+cudaError_t launch_fwd_f16(int D, bool causal, int tile_cfg, const CUtensorMap& tq, const CUtensorMap& tk,
+                           const CUtensorMap& tv, const FwdArgs& a, cudaStream_t s);
+cudaError_t launch_bwd_dq_f16(int D, bool causal, int tile_cfg, const CUtensorMap& tq, const CUtensorMap& tk,
+                              const CUtensorMap& tv, const CUtensorMap& tdo, const BwdArgs& a, cudaStream_t s);
+cudaError_t launch_bwd_dkdv_f16(int D, bool causal, int tile_cfg, const CUtensorMap& tq, const CUtensorMap& tk,
+                                const CUtensorMap& tv, const CUtensorMap& tdo, const BwdArgs& a, cudaStream_t s);
+
+// SIMT kernels (fp32 inputs; any strides).
+cudaError_t launch_fwd_f32(int D, bool causal, const void* q, const void* k, const void* v, Strides4 sq,
+                           Strides4 sk, Strides4 sv, const FwdArgs& a, float sm_scale, cudaStream_t s);
+cudaError_t launch_bwd_dq_f32(int D, bool causal, const BwdArgs& a, cudaStream_t s);
+cudaError_t launch_bwd_dkdv_f32(int D, bool causal, const BwdArgs& a, cudaStream_t s);
+
+// delta = rowsum(dO * O) in fp32 (fp16 or fp32 inputs).
+cudaError_t launch_bwd_preprocess(int D, bool is_f16, const BwdArgs& a, cudaStream_t s);
+
+}  // namespace tattn

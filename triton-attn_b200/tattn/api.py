@@ -1,0 +1,203 @@
+"""Public API: ``attention(q, k, v, causal=False, sm_scale=None)`` with autograd.
+
+Drop-in for the reference's ``src/tattn/api.py``: same signature, the same input validation and
+error messages (api.py:45-56), the same default scale (api.py:182), the same autograd contract
+(api.py:149-173: saves q, k, v, O and the per-row base-2 log-sum-exp M; the backward is
+once-differentiable and returns no gradient for ``causal``/``sm_scale``), and the same private
+``_forward`` / ``_backward`` hooks with an explicit tile ``config`` (api.py:69-146) that tests use to
+check every tile variant. What changes is underneath: each kernel launch goes through the C ABI of
+``libtattn_b200.so`` (include/tattn.h) to hand-written sm_100a CUDA. There is no CPU path: a
+non-CUDA tensor, or a missing library, raises.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Any
+
+import torch
+from torch.autograd.function import once_differentiable
+
+from tattn import _lib
+
+# Tile variants per kernel family, in tile_cfg order (index 0 is the default). They stand in for the
+# reference's autotune spaces (kernels.py:21-41); "BLOCK_M" is the query rows a CTA owns, "BLOCK_N"
+# the keys per inner step.
+TILE_CONFIGS: dict[str, list[dict[str, int]]] = {
+    "fwd": [{"BLOCK_M": 256, "BLOCK_N": 128}],
+    "bwd": [{"BLOCK_M": 128, "BLOCK_N": 64}],
+}
+
+
+def _check(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
+    """Argument validation with the reference's messages (api.py:45-56)."""
+    if q.dim() != 4 or k.shape != q.shape or v.shape != q.shape:
+        raise ValueError(
+            f"expected q, k, v of equal shape [batch, heads, seq, dim]; got {q.shape}, {k.shape}, {v.shape}"
+        )
+    if not (q.device == k.device == v.device):
+        raise ValueError(f"q, k, v must be on one device, got {q.device}, {k.device}, {v.device}")
+    d = q.shape[-1]
+    if d not in (16, 32, 64, 128):
+        raise ValueError(f"head dim must be 16, 32, 64 or 128, got {d}")
+    if not (q.dtype == k.dtype == v.dtype) or q.dtype not in (torch.float16, torch.float32):
+        raise ValueError(f"q, k, v must share dtype float16 or float32, got {q.dtype}, {k.dtype}, {v.dtype}")
+
+
+def cuda_available(device: torch.device) -> bool:
+    """True when ``device`` is a CUDA sm_100 device and the native library loads."""
+    if device.type != "cuda" or not torch.cuda.is_available():
+        return False
+    if torch.cuda.get_device_capability(device)[0] != 10:
+        return False
+    try:
+        _lib.load()
+    except (RuntimeError, OSError):
+        return False
+    return True
+
+
+def triton_available(device: torch.device) -> bool:
+    """Kept for API compatibility with the reference (api.py:35-42): this build has no Triton, so it
+    reports whether the native sm_100 path can run on ``device``."""
+    return cuda_available(device)
+
+
+def _require_cuda(t: torch.Tensor) -> None:
+    if t.device.type != "cuda":
+        raise RuntimeError(
+            f"tattn_b200 runs only on CUDA sm_100 devices (got a tensor on {t.device}); there is no CPU path"
+        )
+
+
+def _tile_cfg(config: dict[str, int] | None, kind: str) -> int:
+    """Map a reference-style tile ``config`` (or {"tile_cfg": i}) to the library's tile index."""
+    if config is None:
+        return 0
+    if "tile_cfg" in config:
+        idx = int(config["tile_cfg"])
+        if not 0 <= idx < len(TILE_CONFIGS[kind]):
+            raise ValueError(f"tile_cfg {idx} out of range for {kind}")
+        return idx
+    want = {key: config[key] for key in ("BLOCK_M", "BLOCK_N") if key in config}
+    for idx, cand in enumerate(TILE_CONFIGS[kind]):
+        if all(cand.get(key) == val for key, val in want.items()):
+            return idx
+    raise ValueError(f"no {kind} tile variant matches {config}; available: {TILE_CONFIGS[kind]}")
+
+
+def _strides(t: torch.Tensor) -> tuple[int, ...]:
+    return tuple(t.stride())
+
+
+def _tma_ready(t: torch.Tensor) -> torch.Tensor:
+    """fp16 tensors are read through TMA: keep them in place when the library can address them,
+    otherwise make a dense, aligned copy (the reference makes such copies too, api.py:111)."""
+    lib = _lib.load()
+    z, h, n, d = t.shape
+    if lib.tattn_layout_ok(t.data_ptr(), _lib.strides_array(_strides(t)), z, h, n, d):
+        return t
+    c = t.contiguous()
+    if c.data_ptr() % 16 != 0:
+        c = torch.empty_like(c, memory_format=torch.contiguous_format).copy_(c)
+    return c
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    return _lib.TATTN_F16 if t.dtype == torch.float16 else _lib.TATTN_F32
+
+
+def _forward(
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool, scale: float,
+    config: dict[str, int] | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:  # fmt: skip
+    """Returns (O, M): O like q (``empty_like``, api.py:87), M fp32 [Z, H, N] (api.py:88)."""
+    _require_cuda(q)
+    lib = _lib.load()
+    z, h, n, d = q.shape
+    tile = _tile_cfg(config, "fwd")
+    if q.dtype == torch.float16:
+        q, k, v = (_tma_ready(t) for t in (q, k, v))
+    o = torch.empty_like(q)
+    if q.dtype == torch.float16 and not lib.tattn_layout_ok(o.data_ptr(), _lib.strides_array(_strides(o)), z, h, n, d):
+        o = torch.empty((z, h, n, d), device=q.device, dtype=q.dtype)
+    m = torch.empty((z, h, n), device=q.device, dtype=torch.float32)
+    strides = _lib.strides_array(_strides(q), _strides(k), _strides(v), _strides(o))
+    with torch.cuda.device(q.device):
+        rc = lib.tattn_fwd(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), m.data_ptr(), strides,
+            z, h, n, d, _dtype_code(q), int(bool(causal)), float(scale), tile, _stream(q),
+        )  # fmt: skip
+    _lib.check("tattn_fwd", rc)
+    return o, m
+
+
+def _backward(
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor, m: torch.Tensor, do: torch.Tensor,
+    causal: bool, scale: float, config: dict[str, int] | None = None,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:  # fmt: skip
+    """Returns contiguous (dq, dk, dv): preprocess -> dK/dV -> dQ, as api.py:102-146."""
+    _require_cuda(q)
+    lib = _lib.load()
+    z, h, n, d = q.shape
+    tile = _tile_cfg(config, "bwd")
+    if q.dtype == torch.float16:
+        q, k, v, do, o = (_tma_ready(t) for t in (q, k, v, do.to(q.dtype), o))
+    else:
+        q, k, v, do, o = (t.contiguous() for t in (q, k, v, do.to(q.dtype), o))
+    m = m.contiguous()
+    delta = torch.empty((z, h, n), device=q.device, dtype=torch.float32)
+    dq = torch.empty((z, h, n, d), device=q.device, dtype=q.dtype)
+    dk = torch.empty_like(dq)
+    dv = torch.empty_like(dq)
+    code, stream, causal_i, sc = _dtype_code(q), _stream(q), int(bool(causal)), float(scale)
+    qkvdo = _lib.strides_array(_strides(q), _strides(k), _strides(v), _strides(do))
+    with torch.cuda.device(q.device):
+        rc = lib.tattn_bwd_preprocess(
+            o.data_ptr(), do.data_ptr(), delta.data_ptr(), _lib.strides_array(_strides(o), _strides(do)),
+            z, h, n, d, code, stream,
+        )  # fmt: skip
+        _lib.check("tattn_bwd_preprocess", rc)
+        rc = lib.tattn_bwd_dkdv(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+            m.data_ptr(), delta.data_ptr(), qkvdo, z, h, n, d, code, causal_i, sc, tile, stream,
+        )  # fmt: skip
+        _lib.check("tattn_bwd_dkdv", rc)
+        rc = lib.tattn_bwd_dq(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), dq.data_ptr(),
+            m.data_ptr(), delta.data_ptr(), qkvdo, z, h, n, d, code, causal_i, sc, tile, stream,
+        )  # fmt: skip
+        _lib.check("tattn_bwd_dq", rc)
+    return dq, dk, dv
+
+
+class _Attention(torch.autograd.Function):
+    @staticmethod
+    def forward(
+        ctx: Any, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool, scale: float
+    ) -> torch.Tensor:
+        o, m = _forward(q, k, v, causal, scale)
+        ctx.save_for_backward(q, k, v, o, m)
+        ctx.causal, ctx.scale = causal, scale
+        return o
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx: Any, do: torch.Tensor) -> tuple[torch.Tensor | None, ...]:
+        q, k, v, o, m = ctx.saved_tensors
+        dq, dk, dv = _backward(q, k, v, o, m, do, ctx.causal, ctx.scale)
+        return dq, dk, dv, None, None
+
+
+def attention(
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False, sm_scale: float | None = None
+) -> torch.Tensor:
+    """Fused attention over [batch, heads, seq, dim] tensors on an sm_100 GPU (api.py:176-184)."""
+    _check(q, k, v)
+    scale = sm_scale if sm_scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    out: torch.Tensor = _Attention.apply(q, k, v, causal, scale)
+    return out
