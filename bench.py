@@ -1,0 +1,458 @@
+"""Benchmark: attention fwd and fwd+bwd TFLOP/s (fp16, head_dim 64) on 1..8 B200s.
+
+One step = one forward + backward of ``tattn.attention`` over one batch (BASELINE config 2 per GPU:
+fp16, B4 H16 N4096 D64, non-causal; ``--config cfg3`` / ``cfg5`` select the causal long-context and
+the scaling configs). Multi-GPU runs shard (batch, head) pairs across ranks with no collective on the
+hot path (weak scaling: every rank runs the config-2 batch); each rank times on the device with CUDA
+events, rank 0 reports the max over ranks. FLOPs follow the reference (bench/bench.py:31-35):
+4*B*H*N^2*D, halved when causal, x3.5 for fwd+bwd.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2|cfg3|cfg5] [--impl reference]
+
+``--impl reference`` times the reference's CPU path (the oracle restatement of
+src/tattn/reference.py's tiled_forward/tiled_backward) on the host cores, on a bounded sample of the
+same workload, and prints the same JSON line with "impl": "reference".
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import multiprocessing as mp
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "triton-attn_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "attention fwd and fwd+bwd TFLOP/s (fp16, hd64) at 1/2/4/8 B200 vs fp16 peak"
+CONFIGS = {
+    # name: (batch per GPU, heads, seq, head_dim, causal)
+    "cfg2": (4, 16, 4096, 64, False),
+    "cfg3": (1, 16, 16384, 64, True),
+    "cfg5": (64, 16, 8192, 64, True),  # scaling config: (batch, head) pairs split over the ranks
+}
+T4_PUBLISHED = {"cfg2": 16.9, "cfg3": 15.9}  # reference fwd+bwd TFLOP/s on a T4
+L2_BYTES = 126 * 2**20
+
+
+def flops(b: int, h: int, n: int, d: int, causal: bool, mode: str) -> float:
+    f = 4.0 * b * h * n * n * d
+    if causal:
+        f /= 2
+    return f * (3.5 if mode == "fwd+bwd" else 1.0)
+
+
+def peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"tflops": p["bf16_tflops"], "tflops_sustained": p.get("bf16_tflops_sustained"),
+                "hbm_gbs": p["hbm_gbs"], "source": "measured"}  # fmt: skip
+    return {"tflops": 1590.0, "tflops_sustained": 1400.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+# ------------------------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock / throttle samples every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")  # fmt: skip
+
+    def __init__(self, gpu_index: int) -> None:
+        self.gpu = gpu_index
+        self.proc: subprocess.Popen | None = None
+        self.lines: list[str] = []
+        self._t: threading.Thread | None = None
+
+    def __enter__(self) -> ClockSampler:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )  # fmt: skip
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self) -> None:
+        assert self.proc is not None and self.proc.stdout is not None
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc) -> None:
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self._t is not None:
+                self._t.join(timeout=2)
+
+    def summary(self) -> dict:
+        sm, mx, reasons, power = [], None, set(), []
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        loaded = [s for s in sm if s > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power) if power else None}  # fmt: skip
+
+
+# ------------------------------------------------------------------------------------------- CPU
+def _cpu_worker(args: tuple) -> float:
+    """Time the oracle's tiled forward+backward on (b, h) pairs [lo, hi) with bounded block counts."""
+    import numpy as np
+
+    from oracle import tiled_backward, tiled_forward
+
+    (b_h, n, d, causal, lo, hi, row_blocks, col_blocks, seed) = args
+    rng = np.random.default_rng(seed + lo)
+    shape = (hi - lo, n, d)
+    q, k, v, do = (rng.standard_normal(shape).astype(np.float16) for _ in range(4))
+    t0 = time.perf_counter()
+    o, m = tiled_forward(q, k, v, causal, row_blocks=row_blocks)
+    t1 = time.perf_counter()
+    tiled_backward(q, k, v, o, m, do, causal, col_blocks=col_blocks)
+    t2 = time.perf_counter()
+    return t1 - t0, t2 - t1
+
+
+def _pair_fraction(nb: int, taken: int, causal: bool, reverse: bool) -> float:
+    """Fraction of the block-pair loop covered by the first `taken` outer blocks (16x16 blocks)."""
+    if not causal:
+        return taken / nb
+    # forward: query block i does i+1 key blocks; backward: key block j does nb-j query blocks.
+    w = [(nb - i) if reverse else (i + 1) for i in range(nb)]
+    return sum(w[:taken]) / sum(w)
+
+
+def cpu_baseline(cfg: str, budget_s: float, workers: int) -> dict:
+    """The reference's CPU path (oracle restatement of reference.py's 16x16-block tiled forward and
+    backward, fp16 inputs upcast to fp32) on a bounded sample of the workload, in `workers` spawned
+    processes that split the (batch, head) pairs. Returns TFLOP/s extrapolated to the full workload."""
+    b, h, n, d, causal = CONFIGS[cfg]
+    pairs = b * h
+    nb = (n + 15) // 16
+    # Probe one block to size the sample so the whole measurement takes about `budget_s`.
+    workers = max(1, min(workers, pairs))
+    ctx = mp.get_context("spawn")
+    bounds = [(pairs * i // workers, pairs * (i + 1) // workers) for i in range(workers)]
+    with ctx.Pool(workers) as pool:
+        probe = pool.map(_cpu_worker, [(pairs, n, d, causal, lo, hi, 1, 1, 0) for lo, hi in bounds])
+        per_blk = max(f + bw for f, bw in probe)
+        take = max(1, min(nb, int(budget_s / max(per_blk, 1e-3))))
+        res = pool.map(_cpu_worker, [(pairs, n, d, causal, lo, hi, take, take, 0) for lo, hi in bounds])
+    t_fwd = max(r[0] for r in res) / _pair_fraction(nb, take, causal, False)
+    t_bwd = max(r[1] for r in res) / _pair_fraction(nb, take, causal, True)
+    total = flops(b, h, n, d, causal, "fwd+bwd")
+    return {
+        "value": total / (t_fwd + t_bwd) / 1e12,
+        "unit": "TFLOP/s",
+        "cores": workers,
+        "kind": "port",
+        "sample": (f"{cfg} all {pairs} (b,h) pairs, first {take} of {nb} 16-row query blocks (fwd) and "
+                   f"key blocks (bwd); time scaled by block-pair count"),  # fmt: skip
+        "fwd_s_extrapolated": t_fwd,
+        "bwd_s_extrapolated": t_bwd,
+    }
+
+
+# ------------------------------------------------------------------------------------------- GPU
+def _kernel_times(q, k, v, do, causal, scale, iters: int) -> dict:
+    """Average device time (CUDA events on the launching stream) of each library kernel."""
+    import torch
+
+    from tattn import _lib, api
+
+    lib = _lib.load()
+    z, h, n, d = q.shape
+    o, m = api._forward(q, k, v, causal, scale)
+    delta = torch.empty((z, h, n), device=q.device, dtype=torch.float32)
+    dq, dk, dv = (torch.empty_like(q) for _ in range(3))
+    st = _lib.strides_array(q.stride(), k.stride(), v.stride(), do.stride())
+    stream = torch.cuda.current_stream().cuda_stream
+    ci = int(causal)
+    calls = {
+        "fwd": lambda: lib.tattn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), m.data_ptr(),
+                                     _lib.strides_array(q.stride(), k.stride(), v.stride(), o.stride()),
+                                     z, h, n, d, 0, ci, scale, 0, stream),
+        "preprocess": lambda: lib.tattn_bwd_preprocess(o.data_ptr(), do.data_ptr(), delta.data_ptr(),
+                                                       _lib.strides_array(o.stride(), do.stride()),
+                                                       z, h, n, d, 0, stream),
+        "dkdv": lambda: lib.tattn_bwd_dkdv(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), dk.data_ptr(),
+                                           dv.data_ptr(), m.data_ptr(), delta.data_ptr(), st, z, h, n, d, 0, ci,
+                                           scale, 0, stream),
+        "dq": lambda: lib.tattn_bwd_dq(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), dq.data_ptr(),
+                                       m.data_ptr(), delta.data_ptr(), st, z, h, n, d, 0, ci, scale, 0, stream),
+    }  # fmt: skip
+    out = {}
+    for name, fn in calls.items():
+        for _ in range(3):
+            _lib.check(name, fn())
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        out[name] = e0.elapsed_time(e1) / iters
+    return out
+
+
+def run_gpu(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from tattn import _lib, attention
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    b, h, n, d, causal = CONFIGS[args.config]
+    if args.config == "cfg5":  # strong scaling of the fixed 1024 (b, h) pairs
+        pairs = b * h
+        lo, hi = pairs * rank // world, pairs * (rank + 1) // world
+        b_local, h_local = 1, hi - lo
+    else:  # weak scaling: each rank runs the whole config on its own (batch, head) shard
+        b_local, h_local = b, h
+    scale = 1.0 / math.sqrt(d)
+    shape = (b_local, h_local, n, d)
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    q, k, v, do = (torch.randn(shape, generator=g, device=dev).to(torch.float16) for _ in range(4))
+    qg, kg, vg = (t.detach().requires_grad_() for t in (q, k, v))
+
+    def step():
+        out = attention(qg, kg, vg, causal=causal)
+        return torch.autograd.grad(out, (qg, kg, vg), do)
+
+    def fwd_only():
+        with torch.no_grad():
+            return attention(q, k, v, causal=causal)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if _lib.device_status() != 0:
+        raise RuntimeError("device status word set during warm-up")
+
+    def timed(fn, iters):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = t.item()
+        return ms
+
+    with ClockSampler(local) as clk:
+        ms_total = timed(step, args.steps)
+    ms_step = ms_total / args.steps
+    for _ in range(3):
+        fwd_only()
+    ms_fwd = timed(fwd_only, args.steps) / args.steps
+
+    # e2e: host (pinned) inputs -> device -> fwd+bwd -> outputs and gradients back to pinned host.
+    host_in = [t.cpu().pin_memory() for t in (q, k, v, do)]
+    host_out = [torch.empty(shape, dtype=torch.float16).pin_memory() for _ in range(4)]
+
+    def e2e_step():
+        dq_, dk_, dv_ = (torch.empty(shape, device=dev, dtype=torch.float16) for _ in range(3))
+        qd, kd, vd, dod = (t.to(dev, non_blocking=True) for t in host_in)
+        qd.requires_grad_()
+        kd.requires_grad_()
+        vd.requires_grad_()
+        out = attention(qd, kd, vd, causal=causal)
+        dq_, dk_, dv_ = torch.autograd.grad(out, (qd, kd, vd), dod)
+        for dst, src in zip(host_out, (out.detach(), dq_, dk_, dv_)):
+            dst.copy_(src, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    ms_e2e = timed(e2e_step, max(3, args.steps // 2)) / max(3, args.steps // 2)
+    if _lib.device_status() != 0:
+        raise RuntimeError("device status word set during the timed region")
+
+    kt = _kernel_times(q, k, v, do, causal, scale, max(5, args.steps))
+    if world > 1:
+        kt_t = torch.tensor([kt[k_] for k_ in sorted(kt)], device=dev, dtype=torch.float64)
+        dist.all_reduce(kt_t, op=dist.ReduceOp.MAX)
+        kt = dict(zip(sorted(kt), kt_t.tolist()))
+
+    per_rank_fb = flops(b_local, h_local, n, d, causal, "fwd+bwd")
+    per_rank_f = flops(b_local, h_local, n, d, causal, "fwd")
+    total_fb = per_rank_fb * world
+    total_f = per_rank_f * world
+    value = total_fb / (ms_step * 1e-3) / 1e12
+    fwd_tflops = total_f / (ms_fwd * 1e-3) / 1e12
+    pk = peaks()
+    # GEMM FLOPs each kernel actually performs per launch (2 flops per MAC; causal halves the pairs).
+    pair_flops = 2.0 * b_local * h_local * n * n * d * (0.5 if causal else 1.0)
+    kflops = {"fwd": 2 * pair_flops, "dkdv": 4 * pair_flops, "dq": 3 * pair_flops}
+    dom = max(("fwd", "dkdv", "dq"), key=lambda kk: kt[kk])
+    achieved = kflops[dom] / (kt[dom] * 1e-3) / 1e12
+    bytes_in = 4 * b_local * h_local * n * d * 2
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True,
+            "scaling": "strong" if args.config == "cfg5" else "weak",
+            "vs_baseline": round(value / T4_PUBLISHED[args.config], 2) if args.config in T4_PUBLISHED else None,
+            "vs_baseline_ref": "reference fwd+bwd on a Tesla T4 (BASELINE.md, results/t4.json)",
+            "dtype": "fp16",
+            "data": "synthetic: q,k,v,dO ~ N(0,1) cast to fp16, seeded per rank",
+            "config": {
+                "workload": f"{args.config}: fp16 fwd+bwd B{b_local} H{h_local} N{n} D{d} "
+                            f"{'causal' if causal else 'non-causal'} per GPU",
+                "global_batch_heads": b_local * h_local * world,
+                "seq_len": n,
+                "head_dim": d,
+                "causal": causal,
+                "parallelism": f"(batch, head) sharding over {world} GPU(s), no collective on the hot path",
+                "l2": f"working set {8 * bytes_in // 4 / 2**20:.0f} MiB per step > 126 MB L2 (inputs larger than L2)",
+            },  # fmt: skip
+            "fwd_tflops": round(fwd_tflops, 2),
+            "fwd_ms": round(ms_fwd, 4),
+            "fwd_frac_of_peak": round(fwd_tflops / world / pk["tflops"], 4),
+            "fwd_bwd_frac_of_peak": round(value / world / pk["tflops"], 4),
+            "peak_tflops_per_gpu": pk["tflops"],
+            "peak_source": f"{pk['source']} (MEASURED_PEAKS.json bf16_tflops, burst; fp16 dense equals bf16)",
+            "kernel_ms": {k_: round(v_, 4) for k_, v_ in kt.items()},
+            "roofline": {
+                "kernel": dom,
+                "bound": "tensor",
+                "achieved": round(achieved, 1),
+                "peak": pk["tflops"],
+                "unit": "TFLOP/s",
+                "frac": round(achieved / pk["tflops"], 4),
+                "traffic": None,
+                "flops_per_launch": kflops[dom],
+            },
+            "e2e": {
+                "value": round(total_fb / (ms_e2e * 1e-3) / 1e12, 2),
+                "unit": "TFLOP/s",
+                "ms_per_step": round(ms_e2e, 3),
+                "h2d_bytes_per_step": bytes_in,
+                "d2h_bytes_per_step": bytes_in,
+                "path": "tattn.attention with pinned host q,k,v,dO copied in and O,dq,dk,dv copied out per step",
+            },
+            "gpu_launches": 4 * args.steps,
+            "clocks": clk.summary(),
+        }
+        if world == 1 and not args.no_cpu:
+            line["cpu_baseline"] = cpu_baseline(args.config, args.cpu_budget, max(1, os.cpu_count() or 1))
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference(args) -> None:
+    """The reference's CPU implementation of the path (oracle port), rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    cores = max(1, os.cpu_count() or 1)
+    vals = []
+    for _ in range(args.warmup):
+        cpu_baseline(args.config, 2.0, cores)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        vals.append(cpu_baseline(args.config, args.cpu_budget / max(1, args.steps), cores))
+    wall = time.perf_counter() - t0
+    b, h, n, d, causal = CONFIGS[args.config]
+    value = statistics.median(v["value"] for v in vals)
+    cb = dict(vals[-1])
+    cb["value"] = round(value, 6)
+    line = {
+        "metric": METRIC,
+        "value": round(value, 6),
+        "unit": "TFLOP/s",
+        "impl": "reference",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(flops(b, h, n, d, causal, "fwd+bwd") / (value * 1e12) * 1e3, 1),
+        "higher_is_better": True,
+        "scaling": "strong" if args.config == "cfg5" else "weak",
+        "vs_baseline": None,
+        "dtype": "fp16 inputs, fp32 arithmetic (reference CPU path)",
+        "data": "synthetic: q,k,v,dO ~ N(0,1) cast to fp16",
+        "config": {"workload": f"{args.config}: fp16 fwd+bwd B{b} H{h} N{n} D{d} {'causal' if causal else 'non-causal'}",
+                   "seq_len": n, "head_dim": d, "causal": causal},  # fmt: skip
+        "cpu_baseline": cb,
+        "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "wall_s": round(wall, 1),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg2")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU work for the CPU baseline")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -97,6 +97,18 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, unsig
   }
 }
 
+// Warp-uniform bounded wait: every lane waits (each gets acquire ordering), then the lanes agree, so
+// the warp stays converged for the .sync.aligned tcgen05 instructions that follow.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const CtaAbort& ab) {
+  const bool ok = mbar_wait(bar, parity, ab);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// Named barrier over `nthreads` threads (a multiple of 32); id 0 is __syncthreads.
+__device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // ----------------------------------------------------------------------------------------------
 // TMA (no multicast anywhere in this library)
 // ----------------------------------------------------------------------------------------------

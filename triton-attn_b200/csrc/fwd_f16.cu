@@ -72,12 +72,6 @@ __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint3
   }
 }
 
-// Warp-uniform bounded wait: every lane waits (each gets acquire ordering), then the lanes agree.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const CtaAbort& ab) {
-  const bool ok = mbar_wait(bar, parity, ab);
-  return __all_sync(0xffffffffu, ok);
-}
-
 template <int D, bool CAUSAL>
 __global__ void __launch_bounds__(320, 1)
     fwd_f16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
