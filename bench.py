@@ -50,6 +50,24 @@ def flops(b: int, h: int, n: int, d: int, causal: bool, mode: str) -> float:
     return f * (3.5 if mode == "fwd+bwd" else 1.0)
 
 
+def shard(pairs: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous (batch, head) pair range [lo, hi) of `rank`: pairs are independent in the forward
+    and the backward, so ranks need no data exchange; sizes differ by at most one pair."""
+    return pairs * rank // world, pairs * (rank + 1) // world
+
+
+def max_over_ranks(ms: float, device=None) -> float:
+    """Device time of the slowest rank (MAX all-reduce of one scalar, outside the timed region)."""
+    import torch
+    import torch.distributed as dist
+
+    if not dist.is_initialized() or dist.get_world_size() == 1:
+        return ms
+    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def peaks() -> dict:
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -245,8 +263,7 @@ def run_gpu(args) -> None:
     torch.cuda.set_device(dev)
     b, h, n, d, causal = CONFIGS[args.config]
     if args.config == "cfg5":  # strong scaling of the fixed 1024 (b, h) pairs
-        pairs = b * h
-        lo, hi = pairs * rank // world, pairs * (rank + 1) // world
+        lo, hi = shard(b * h, rank, world)
         b_local, h_local = 1, hi - lo
     else:  # weak scaling: each rank runs the whole config on its own (batch, head) shard
         b_local, h_local = b, h
@@ -280,16 +297,20 @@ def run_gpu(args) -> None:
             fn()
         e1.record()
         torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1)
-        if world > 1:
-            t = torch.tensor([ms], device=dev, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = t.item()
-        return ms
+        return max_over_ranks(e0.elapsed_time(e1), dev)
 
     with ClockSampler(local) as clk:
         ms_total = timed(step, args.steps)
     ms_step = ms_total / args.steps
+    if args.lean:  # profiling runs: warm-up + timed steps only
+        if rank == 0:
+            total = flops(b_local, h_local, n, d, causal, "fwd+bwd") * world
+            print(json.dumps({"lean": True, "config": args.config, "ms_per_step": ms_step,
+                              "tflops": total / (ms_step * 1e-3) / 1e12}), flush=True)  # fmt: skip
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     for _ in range(3):
         fwd_only()
     ms_fwd = timed(fwd_only, args.steps) / args.steps
@@ -445,6 +466,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU work for the CPU baseline")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--lean", action="store_true", help="warm-up + timed steps only (for profiler runs)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
