@@ -51,7 +51,8 @@ enum tattn_status {
   TATTN_ERR_CUDA = 3,             /* a CUDA runtime/driver call or a launch failed */
   TATTN_ERR_NO_DEVICE = 4,        /* current device is not sm_100 or the TMA encoder is missing */
   TATTN_ERR_DEVICE_STATUS = 5,    /* a kernel recorded a failure in the device status word */
-  TATTN_ERR_UNSUPPORTED = 6       /* valid request this build does not implement */
+  TATTN_ERR_UNSUPPORTED = 6,      /* valid request this build does not implement */
+  TATTN_ERR_TOO_LARGE = 7         /* problem exceeds a fixed-size library buffer (tattn_bwd_noalloc) */
 };
 
 /* Device status word bits (tattn_device_status). */
@@ -84,6 +85,23 @@ TATTN_API int tattn_bwd_dkdv(const void* q, const void* k, const void* v, const 
 TATTN_API int tattn_bwd_dq(const void* q, const void* k, const void* v, const void* dout, void* dq, const float* m,
                  const float* delta, const int64_t* strides, int Z, int H, int N, int D, int dtype, int causal,
                  float sm_scale, int tile_cfg, void* stream);
+
+/* Largest Z*H*N accepted by tattn_bwd_noalloc (its fixed fp32 row buffer: 16 MiB per GPU). */
+#define TATTN_BWD_NOALLOC_MAX_ROWS 4194304
+
+/* The whole backward (delta preprocess, dK/dV, dQ) in one call that allocates no device memory.
+ * No counterpart in the reference: it exists for callers that cannot provide the fp32 row buffer
+ * (delta) the three-call backward needs -- e.g. runtimes that hand out every device byte from a fixed,
+ * pre-planned arena, or host bindings that can only pass the buffers their user gave them. delta lives
+ * instead in a file-scope device array of TATTN_BWD_NOALLOC_MAX_ROWS floats that every GPU loading this
+ * library holds until exit; larger problems return TATTN_ERR_TOO_LARGE. All calls on a device share
+ * that array: each call rewrites every entry it reads, but calls that overlap on the GPU (unordered
+ * streams) race on it. The first call on a device resolves the array's address; make it before any
+ * stream capture. strides: 20 int64 = q, k, v, o, dout each (z, h, n, d); dq, dk, dv: dense
+ * [Z, H, N, D]; other conventions as tattn_bwd_dkdv / tattn_bwd_dq (tile_cfg 0). */
+TATTN_API int tattn_bwd_noalloc(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                                void* dq, void* dk, void* dv, const float* m, const int64_t* strides, int Z,
+                                int H, int N, int D, int dtype, int causal, float sm_scale, void* stream);
 
 /* Can the fp16 tensor-core path read this tensor in place? Returns 1 (yes) or 0 (make it contiguous).
  * strides: 4 int64 (z, h, n, d). Mirrors the check every fp16 entry point applies. */

@@ -298,6 +298,7 @@ extern "C" const char* tattn_status_string(int status) {
     case TATTN_ERR_NO_DEVICE: return "current device is not an sm_100 GPU (or the TMA encoder is unavailable)";
     case TATTN_ERR_DEVICE_STATUS: return "a kernel recorded a failure in the device status word";
     case TATTN_ERR_UNSUPPORTED: return "not implemented by this build";
+    case TATTN_ERR_TOO_LARGE: return "problem larger than the fixed no-allocation buffer (Z*H*N > TATTN_BWD_NOALLOC_MAX_ROWS)";
     default: return "unknown status";
   }
 }

@@ -15,6 +15,8 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), LIB_NAME)
 
 TATTN_F16, TATTN_F32 = 0, 1
 OK, ERR_INVALID_ARGUMENT, ERR_LAYOUT, ERR_CUDA, ERR_NO_DEVICE, ERR_DEVICE_STATUS, ERR_UNSUPPORTED = range(7)
+ERR_TOO_LARGE = 7
+BWD_NOALLOC_MAX_ROWS = 4194304  # TATTN_BWD_NOALLOC_MAX_ROWS
 
 # Every symbol include/tattn.h declares, with its ctypes signature.
 _P, _I, _F, _I64P = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.POINTER(ctypes.c_int64)
@@ -23,6 +25,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tattn_bwd_preprocess": (_I, [_P, _P, _P, _I64P, _I, _I, _I, _I, _I, _P]),
     "tattn_bwd_dkdv": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I64P, _I, _I, _I, _I, _I, _I, _F, _I, _P]),
     "tattn_bwd_dq": (_I, [_P, _P, _P, _P, _P, _P, _P, _I64P, _I, _I, _I, _I, _I, _I, _F, _I, _P]),
+    "tattn_bwd_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64P, _I, _I, _I, _I, _I, _I, _F, _P]),
     "tattn_layout_ok": (_I, [_P, _I64P, _I, _I, _I, _I]),
     "tattn_tile_configs": (_I, [_I]),
     "tattn_device_status": (_I, [_P, ctypes.POINTER(ctypes.c_int), _I]),
