@@ -111,6 +111,11 @@ TATTN_API int tattn_layout_ok(const void* ptr, const int64_t* strides, int Z, in
  * 1 = backward. Stands in for the reference's autotune spaces (kernels.py:21-41); 0 is the default. */
 TATTN_API int tattn_tile_configs(int kind);
 
+/* Diagnostic (no reference counterpart): evaluate, for n inputs x, the FMA-pipe exp2 the kernels use
+ * for part of each softmax row (y_poly), the hardware ex2.approx (y_hw) and CUDA's exp2f (y_lib), so
+ * a test can hold the polynomial to its error bound against CUDA's own outputs. Device pointers. */
+TATTN_API int tattn_selftest_exp2(const float* x, float* y_poly, float* y_hw, float* y_lib, int n, void* stream);
+
 /* Synchronise `stream`, then report the current device's status word (TATTN_DEV_* bits) in *out and
  * clear it when `clear` is nonzero. Returns TATTN_OK, or TATTN_ERR_CUDA if the sync failed. */
 TATTN_API int tattn_device_status(void* stream, int* out, int clear);

@@ -266,3 +266,31 @@ def test_full_size_properties() -> None:
         ab, _ = api._forward(q, k, (v1.float() * 0.5 + v2.float() * 0.25).half(), causal, 0.125)
         lin = a.float() * 0.5 + bb.float() * 0.25
         assert (ab.float() - lin).abs().max().item() <= 2e-3
+
+
+# --------------------------------------------------------------------------------- FMA-pipe exp2
+def test_polynomial_exp2_against_cuda() -> None:
+    """The kernels' FMA-pipe exp2 (Cody-Waite reduction + Remez cubic, csrc/fit_exp2_poly.py) against
+    CUDA's exp2f and the hardware ex2.approx, and against its 7.5e-5 relative error bound, over the
+    range the softmax feeds it (x <= 8), including underflow and -inf."""
+    lib = _lib.load()
+    x = torch.cat([
+        torch.linspace(-30.0, 8.0, 400_001),
+        torch.tensor([0.0, -0.5, 0.5, -1.0, 1.0, 8.0, -24.0, -125.9, -126.0, -126.5, -127.0, -200.0, -1e30,
+                      float("-inf")]),
+    ]).cuda()  # fmt: skip
+    yp, yh, yl = (torch.empty_like(x) for _ in range(3))
+    _lib.check("tattn_selftest_exp2", lib.tattn_selftest_exp2(x.data_ptr(), yp.data_ptr(), yh.data_ptr(),
+                                                            yl.data_ptr(), x.numel(), None))
+    torch.cuda.synchronize()
+    exact = torch.exp2(x.double().cpu())
+    p, lib_y, hw = yp.double().cpu(), yl.double().cpu(), yh.double().cpu()
+    normal = x.cpu() >= -24.0  # results that survive in an fp16 P
+    rel = ((p - exact).abs() / exact)[normal]
+    assert rel.max().item() < 8e-5, rel.max().item()
+    rel_lib = ((p - lib_y).abs() / lib_y)[normal]
+    assert rel_lib.max().item() < 8e-5, rel_lib.max().item()
+    rel_hw = ((p - hw).abs() / hw)[normal]
+    assert rel_hw.max().item() < 1e-4, rel_hw.max().item()
+    tiny = ~normal
+    assert torch.isfinite(p[tiny]).all() and (p[tiny] >= 0).all() and (p[tiny] <= 2.0**-23).all()

@@ -607,6 +607,13 @@ cudaError_t dkdv_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtens
 
 }  // namespace
 
+void bwd_f16_box_rows(bool dq_pass, int* q_rows, int* kv_rows) {
+  // dQ: 128-row query tiles, DqCfg::BN-row key blocks; dK/dV: 128-row key tiles, DkvCfg::BQ-row query
+  // blocks (the same for every head dim).
+  *q_rows = dq_pass ? 128 : DkvCfg<64>::BQ;
+  *kv_rows = dq_pass ? DqCfg<64>::BN : 128;
+}
+
 #define TATTN_BWD_SWITCH(FN)                                                                  \
   switch (D) {                                                                                \
     case 16: return causal ? FN<16, true>(tq, tk, tv, tdo, a, s) : FN<16, false>(tq, tk, tv, tdo, a, s);   \

@@ -154,9 +154,10 @@ extern "C" int tattn_fwd(const void* q, const void* k, const void* v, void* o, f
   a.qk_scale = (sm_scale < 0.f ? -sm_scale : sm_scale) * kLog2e;
   a.negate_s = sm_scale < 0.f ? 1 : 0;
   CUtensorMap tq, tk, tv;
+  const int kv_rows = fwd_f16_kv_rows(D);  // must match the kernel's K/V shared-memory slots
   if ((rc = encode_f16(&tq, q, sq, Z, H, N, D, 128)) != TATTN_OK) return rc;
-  if ((rc = encode_f16(&tk, k, sk, Z, H, N, D, 128)) != TATTN_OK) return rc;
-  if ((rc = encode_f16(&tv, v, sv, Z, H, N, D, 128)) != TATTN_OK) return rc;
+  if ((rc = encode_f16(&tk, k, sk, Z, H, N, D, kv_rows)) != TATTN_OK) return rc;
+  if ((rc = encode_f16(&tv, v, sv, Z, H, N, D, kv_rows)) != TATTN_OK) return rc;
   return cuda_rc(launch_fwd_f16(D, causal != 0, tile_cfg, tq, tk, tv, a, s));
 }
 
@@ -240,7 +241,8 @@ int bwd_common(bool dq_pass, const void* q, const void* k, const void* v, const 
   (void)dense_n;
   CUtensorMap tq, tk, tv, tdo;
   // dQ: query tiles of 128 rows, key blocks of 64 rows; dK/dV: key tiles of 128 rows, query blocks of 64.
-  const int q_rows = dq_pass ? 128 : 64, kv_rows = dq_pass ? 64 : 128;
+  int q_rows = 0, kv_rows = 0;
+  bwd_f16_box_rows(dq_pass, &q_rows, &kv_rows);  // must match the kernels' shared-memory slots
   if ((rc = encode_f16(&tq, q, a.sq, Z, H, N, D, q_rows)) != TATTN_OK) return rc;
   if ((rc = encode_f16(&tk, k, a.sk, Z, H, N, D, kv_rows)) != TATTN_OK) return rc;
   if ((rc = encode_f16(&tv, v, a.sv, Z, H, N, D, kv_rows)) != TATTN_OK) return rc;

@@ -283,4 +283,59 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// ---- packed fp32 pairs (sm_100 f32x2 instructions: one issue slot for two lanes' worth of math)
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 f2_unpack(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t fsub2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for a pair on the FMA/ALU pipes, leaving MUFU free for the other exponentials of a row.
+// Method: Cody-Waite style reduction x = j + f with j = round-to-nearest(x) obtained by adding the
+// shifter 1.5*2^23 (j lands in the low mantissa bits of t = x + shifter), f = x - j in [-0.5, 0.5];
+// 2^f by a degree-3 polynomial minimising the maximum relative error on [-0.5, 0.5] (Remez exchange;
+// coefficients derived by csrc/fit_exp2_poly.py, max relative error 7.5e-5), then 2^j applied by adding
+// j << 23 to the result's exponent field. x is clamped to >= -126 so the exponent never underflows;
+// results below 2^-24 vanish in the fp16 P anyway. Valid for x <= 127 (callers pass x <= 8).
+__device__ __forceinline__ uint64_t exp2_poly_x2(uint64_t x2) {
+  float2 x = f2_unpack(x2);
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
+  const uint64_t xc = f2(x.x, x.y);
+  const uint64_t shifter = f2(12582912.f, 12582912.f);
+  const uint64_t t = fadd2(xc, shifter);
+  const uint64_t f = fsub2(xc, fsub2(t, shifter));
+  uint64_t p = ffma2(f2(0.0551716685295105f, 0.0551716685295105f), f, f2(0.2426111251115799f, 0.2426111251115799f));
+  p = ffma2(p, f, f2(0.6932609677314758f, 0.6932609677314758f));
+  p = ffma2(p, f, f2(0.9999280571937561f, 0.9999280571937561f));
+  const float2 pv = f2_unpack(p), tv = f2_unpack(t);
+  return f2(__int_as_float(__float_as_int(pv.x) + (__float_as_int(tv.x) << 23)),
+            __int_as_float(__float_as_int(pv.y) + (__float_as_int(tv.y) << 23)));
+}
+
 }  // namespace tattn

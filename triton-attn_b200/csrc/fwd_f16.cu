@@ -2,18 +2,21 @@
 // accumulators, warp-specialised roles.
 //
 // Algorithm (the reference's _fwd_kernel, src/tattn/kernels.py:57-148): for each 128-row query tile,
-// loop over 128-key blocks, S = Q K^T, online softmax in base 2 (scores scaled by sm_scale*log2(e),
-// exp2), O = sum(P V) / l, and M = m + log2(l) saved per row. Causal tiles stop at the diagonal block.
+// loop over key blocks, S = Q K^T, online softmax in base 2 (scores scaled by sm_scale*log2(e), exp2),
+// O = sum(P V) / l, and M = m + log2(l) saved per row. Causal tiles stop at the diagonal block.
 //
-// B200 mapping (one CTA per SM, 320 threads):
-//   warps 0-3  softmax warpgroup for query tile 0 (thread t owns TMEM lane t = query row t)
-//   warps 4-7  softmax warpgroup for query tile 1
-//   warp 8     TMA producer: Q tiles once, then K/V blocks through an NS-stage ring
-//   warp 9     TMEM allocator + MMA issuer (one thread)
-// TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D). P (fp16) overwrites the
-// first 64 columns of its S buffer and is the A operand of the PV MMA straight from TMEM.
-// The two softmax warpgroups ping-pong: while one exponentiates its S tile, the tensor core runs the
-// other tile's PV and next QK^T.
+// B200 mapping (one CTA per SM, 384 threads = 3 warpgroups):
+//   warpgroup 0 (warps 0-3)   softmax for query tile 0 (thread t owns TMEM lane t = query row t)
+//   warpgroup 1 (warps 4-7)   softmax for query tile 1
+//   warpgroup 2: warp 8       TMA producer (Q tiles once, then K/V blocks through an NS-stage ring)
+//                warp 9       TMEM allocator + MMA issuer (one thread, event loop)
+//                warps 10-11  idle (they complete the warpgroup for the register split)
+// setmaxnreg moves registers from warpgroup 2 (48 per thread) to the softmax warpgroups (224), so a
+// softmax thread keeps its whole score row in registers and reads S from TMEM once.
+// TMEM (512 columns): S0, S1 [BN each] | P0, P1 [BN/2 each, fp16 pairs] | O0, O1 [D each]. P has its own
+// buffer, so the tensor core computes S(j+1) of a tile while that tile's softmax still exponentiates
+// S(j): as soon as a softmax warpgroup has S(j) in registers it releases the S buffer (s_free), and
+// the MMA issuer starts the next QK^T. P then feeds the PV MMA as the A operand straight from TMEM.
 // The running max is rescaled lazily: O (in TMEM) and l are only corrected when a row's max grows by
 // more than kRescaleThreshold (log2 units); P values stay below 2^kRescaleThreshold, exact in fp16.
 #include "common.cuh"
@@ -23,29 +26,41 @@ namespace tattn {
 namespace {
 
 constexpr float kRescaleThreshold = 8.0f;
+// Of every 8 column pairs of a row, this many take exp2 on the FMA pipe (exp2_poly_x2) and the rest
+// on MUFU (16 results/clk/SM), whose rate alone caps the D = 64 forward near half the tensor rate.
+constexpr int kEmuPairs = 0;
+// Register split (setmaxnreg): launch = 384 threads x 168 registers = 64512; softmax warpgroups take
+// 224 and warpgroup 2 keeps 48: 8*32*224 + 4*32*48 = 63488 <= 64512.
+constexpr int kSoftmaxRegs = 224;
+constexpr int kProducerRegs = 48;
 
 template <int D>
 struct FwdCfg {
   static constexpr int BM = 128;                        // rows per query tile (2 tiles per CTA)
-  static constexpr int BN = 128;                        // keys per block
-  static constexpr int NS = D <= 64 ? 3 : 2;            // K/V ring depth
+  static constexpr int BN = D == 128 ? 64 : 128;        // keys per block
+  static constexpr int NS = 4;                          // K/V ring depth
   static constexpr int CW = D < 64 ? D : 64;            // columns per swizzle chunk
   static constexpr int NCH = D / CW;                    // chunks per row (2 for D = 128)
   static constexpr int SWB = CW * 2;                    // swizzle span in bytes (32/64/128)
   static constexpr uint32_t LAYOUT = SWB == 128 ? 2u : (SWB == 64 ? 4u : 6u);
-  static constexpr int CHUNK_BYTES = 128 * SWB;         // one 128-row chunk
-  static constexpr int TILE_BYTES = CHUNK_BYTES * NCH;  // one [128, D] fp16 tile
+  static constexpr int QCHUNK = BM * SWB;               // one 128-row chunk
+  static constexpr int QTILE = QCHUNK * NCH;            // one [128, D] fp16 query tile
+  static constexpr int KCHUNK = BN * SWB;               // one BN-row chunk
+  static constexpr int KTILE = KCHUNK * NCH;            // one [BN, D] fp16 key / value block
   static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = 2 * TILE_BYTES;
-  static constexpr int OFF_V = OFF_K + NS * TILE_BYTES;
-  static constexpr int OFF_BAR = OFF_V + NS * TILE_BYTES;
-  // barriers: q_full, k_full[NS], v_full[NS], kv_empty[NS], s_full[2], p_full[2], o_done[2], fin
-  static constexpr int NBARS = 1 + 3 * NS + 7;
+  static constexpr int OFF_K = 2 * QTILE;
+  static constexpr int OFF_V = OFF_K + NS * KTILE;
+  static constexpr int OFF_BAR = OFF_V + NS * KTILE;
+  // q_full, k_full[NS], v_full[NS], kv_empty[NS], s_full[2], s_free[2], p_full[2], o_done[2], fin
+  static constexpr int NBARS = 1 + 3 * NS + 9;
   static constexpr int OFF_MISC = OFF_BAR + NBARS * 8;  // tmem base (u32), abort flag (int)
   static constexpr int SMEM_USED = OFF_MISC + 16;
   // Request at least ~116 KB so exactly one CTA (which owns all 512 TMEM columns) fits per SM.
   static constexpr int SMEM_BYTES = (SMEM_USED > 118784 ? SMEM_USED : 118784) + 1024;
-  static constexpr uint32_t TM_S0 = 0, TM_S1 = 128, TM_O0 = 256, TM_O1 = 256 + D;
+  static constexpr uint32_t TM_S = 0;                   // + i * BN
+  static constexpr uint32_t TM_P = 2 * BN;              // + i * BN / 2
+  static constexpr uint32_t TM_O = 3 * BN;              // + i * D
+  static_assert(3 * BN + 2 * D <= 512, "TMEM budget");
   static constexpr uint32_t IDESC_S = idesc_f16_f32(128, BN, false);
   static constexpr uint32_t IDESC_PV = idesc_f16_f32(128, D, true);
 };
@@ -55,9 +70,9 @@ __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_base, uint3
   using C = FwdCfg<D>;
 #pragma unroll
   for (int kk = 0; kk < D / 16; ++kk) {
-    const uint32_t off = (kk * 16 / C::CW) * C::CHUNK_BYTES + ((kk * 16) % C::CW) * 2;
-    const uint64_t a = smem_desc(q_base + off, 16, 8 * C::SWB, C::LAYOUT);
-    const uint64_t b = smem_desc(k_base + off, 16, 8 * C::SWB, C::LAYOUT);
+    const uint32_t col = kk * 16 / C::CW, inner = ((kk * 16) % C::CW) * 2;
+    const uint64_t a = smem_desc(q_base + col * C::QCHUNK + inner, 16, 8 * C::SWB, C::LAYOUT);
+    const uint64_t b = smem_desc(k_base + col * C::KCHUNK + inner, 16, 8 * C::SWB, C::LAYOUT);
     mma_f16_ss(d_tmem, a, b, idesc, kk > 0 ? 1u : 0u);
   }
 }
@@ -67,16 +82,29 @@ __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint3
   using C = FwdCfg<D>;
 #pragma unroll
   for (int kk = 0; kk < C::BN / 16; ++kk) {
-    const uint64_t b = smem_desc(v_base + kk * 16 * C::SWB, C::CHUNK_BYTES, 8 * C::SWB, C::LAYOUT);
+    const uint64_t b = smem_desc(v_base + kk * 16 * C::SWB, C::KCHUNK, 8 * C::SWB, C::LAYOUT);
     mma_f16_ts(d_tmem, p_tmem + kk * 8, b, C::IDESC_PV, (accumulate || kk > 0) ? 1u : 0u);
   }
 }
 
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 template <int D, bool CAUSAL>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(384, 1)
     fwd_f16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const FwdArgs args) {
   using C = FwdCfg<D>;
+  constexpr int BN = C::BN;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
   const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
@@ -88,9 +116,10 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* bar_v_full = bars + 1 + C::NS;
   uint64_t* bar_kv_empty = bars + 1 + 2 * C::NS;
   uint64_t* bar_s_full = bars + 1 + 3 * C::NS;
-  uint64_t* bar_p_full = bar_s_full + 2;
-  uint64_t* bar_o_done = bar_s_full + 4;
-  uint64_t* bar_fin = bar_s_full + 6;
+  uint64_t* bar_s_free = bar_s_full + 2;
+  uint64_t* bar_p_full = bar_s_full + 4;
+  uint64_t* bar_o_done = bar_s_full + 6;
+  uint64_t* bar_fin = bar_s_full + 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
   const CtaAbort ab{abort_flag, args.status};
@@ -107,14 +136,12 @@ __global__ void __launch_bounds__(320, 1)
     cta = blockIdx.x % nct;
   }
   const int zi = bh / args.H, hi = bh % args.H;
-  const int NB = (N + C::BN - 1) / C::BN;
-  int row0[2], nblk[2];
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    row0[i] = (2 * cta + i) * C::BM;
-    nblk[i] = row0[i] >= N ? 0 : (CAUSAL ? min(2 * cta + i + 1, NB) : NB);
-  }
-  const int nmax = max(nblk[0], nblk[1]);
+  const int NB = (N + BN - 1) / BN;
+  // Query tile i of this CTA: rows [row0_i, row0_i + 128), key blocks [0, n_i).
+  const int row0_0 = 2 * cta * C::BM, row0_1 = row0_0 + C::BM;
+  const int n_0 = row0_0 >= N ? 0 : (CAUSAL ? min((row0_0 + C::BM + BN - 1) / BN, NB) : NB);
+  const int n_1 = row0_1 >= N ? 0 : (CAUSAL ? min((row0_1 + C::BM + BN - 1) / BN, NB) : NB);
+  const int nmax = max(n_0, n_1);
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q, 1);
@@ -125,6 +152,7 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar_s_full[i], 1);
+      mbar_init(&bar_s_free[i], 128);
       mbar_init(&bar_p_full[i], 128);
       mbar_init(&bar_o_done[i], 1);
     }
@@ -148,29 +176,27 @@ __global__ void __launch_bounds__(320, 1)
 
   const uint32_t sQ = base_u32 + C::OFF_Q, sK = base_u32 + C::OFF_K, sV = base_u32 + C::OFF_V;
 
-  if (warp == 8) {
-    // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      uint32_t qbytes = 0;
-      for (int i = 0; i < 2; ++i) qbytes += nblk[i] > 0 ? C::TILE_BYTES : 0;
+  if (warp >= 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
+    if (warp == 8 && lane == 0) {
+      // -------------------------------------------------------------- TMA producer
+      const uint32_t qbytes = (n_0 > 0 ? C::QTILE : 0) + (n_1 > 0 ? C::QTILE : 0);
       mbar_arrive_expect_tx(bar_q, qbytes);
       for (int i = 0; i < 2; ++i) {
-        if (nblk[i] == 0) continue;
+        if ((i ? n_1 : n_0) == 0) continue;
         for (int ch = 0; ch < C::NCH; ++ch)
-          tma_load_4d(sQ + i * C::TILE_BYTES + ch * C::CHUNK_BYTES, &tm_q, ch * C::CW, row0[i], hi, zi, bar_q);
+          tma_load_4d(sQ + i * C::QTILE + ch * C::QCHUNK, &tm_q, ch * C::CW, i ? row0_1 : row0_0, hi, zi, bar_q);
       }
       int j = 0;
       for (; j < nmax; ++j) {
         const int st = j % C::NS;
         if (j >= C::NS && !mbar_wait(&bar_kv_empty[st], ((j / C::NS) - 1) & 1, ab)) break;
-        mbar_arrive_expect_tx(&bar_k_full[st], C::TILE_BYTES);
+        mbar_arrive_expect_tx(&bar_k_full[st], C::KTILE);
         for (int ch = 0; ch < C::NCH; ++ch)
-          tma_load_4d(sK + st * C::TILE_BYTES + ch * C::CHUNK_BYTES, &tm_k, ch * C::CW, j * C::BN, hi, zi,
-                      &bar_k_full[st]);
-        mbar_arrive_expect_tx(&bar_v_full[st], C::TILE_BYTES);
+          tma_load_4d(sK + st * C::KTILE + ch * C::KCHUNK, &tm_k, ch * C::CW, j * BN, hi, zi, &bar_k_full[st]);
+        mbar_arrive_expect_tx(&bar_v_full[st], C::KTILE);
         for (int ch = 0; ch < C::NCH; ++ch)
-          tma_load_4d(sV + st * C::TILE_BYTES + ch * C::CHUNK_BYTES, &tm_v, ch * C::CW, j * C::BN, hi, zi,
-                      &bar_v_full[st]);
+          tma_load_4d(sV + st * C::KTILE + ch * C::KCHUNK, &tm_v, ch * C::CW, j * BN, hi, zi, &bar_v_full[st]);
       }
       // Every copy this CTA issued must land before the CTA exits (instant on the normal path).
       const unsigned long long lim = 100ull * 1000ull * 1000ull;
@@ -179,42 +205,56 @@ __global__ void __launch_bounds__(320, 1)
         mbar_drain(&bar_k_full[jj % C::NS], (jj / C::NS) & 1, lim);
         mbar_drain(&bar_v_full[jj % C::NS], (jj / C::NS) & 1, lim);
       }
-    }
-  } else if (warp == 9) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    } else if (warp == 9 && lane == 0) {
+      // -------------------------------------------------------------- MMA issuer (event loop)
+      // Per tile: S(b) needs the tile's S buffer released (s_free of b-1) and K(b); PV(b) needs P(b)
+      // (p_full of b) and V(b). Whatever is ready is issued; a K/V stage is released once every tile
+      // that uses block b has issued PV(b).
       const uint32_t idesc_s = C::IDESC_S | (args.negate_s ? (1u << 13) : 0u);
-      const uint32_t tS[2] = {tmem + C::TM_S0, tmem + C::TM_S1};
-      const uint32_t tO[2] = {tmem + C::TM_O0, tmem + C::TM_O1};
       bool ok = mbar_wait(bar_q, 0, ab);
-      if (ok && nmax > 0) ok = mbar_wait(&bar_k_full[0], 0, ab);
-      if (ok) {
-        tc_fence_after();
+      int next_s0 = 0, next_s1 = 0, next_pv0 = 0, next_pv1 = 0, released = 0;
+      unsigned long long idle_since = 0;
+      while (ok && (next_pv0 < n_0 || next_pv1 < n_1)) {
+        bool progress = false;
+#pragma unroll
         for (int i = 0; i < 2; ++i) {
-          if (nblk[i] == 0) continue;
-          issue_qk<D>(tS[i], sQ + i * C::TILE_BYTES, sK, idesc_s);
-          mma_commit(&bar_s_full[i]);
-        }
-      }
-      for (int j = 0; ok && j < nmax; ++j) {
-        const int st = j % C::NS;
-        if (!mbar_wait(&bar_v_full[st], (j / C::NS) & 1, ab)) { ok = false; break; }
-        for (int i = 0; i < 2 && ok; ++i) {
-          if (j >= nblk[i]) continue;
-          if (!mbar_wait(&bar_p_full[i], j & 1, ab)) { ok = false; break; }
-          tc_fence_after();
-          issue_pv<D>(tO[i], tS[i], sV + st * C::TILE_BYTES, j > 0);
-          mma_commit(&bar_o_done[i]);
-          if (j + 1 < nblk[i]) {
-            const int st1 = (j + 1) % C::NS;
-            if (!mbar_wait(&bar_k_full[st1], ((j + 1) / C::NS) & 1, ab)) { ok = false; break; }
+          const int n = i ? n_1 : n_0;
+          int& ns = i ? next_s1 : next_s0;
+          int& np = i ? next_pv1 : next_pv0;
+          if (ns < n && (ns == 0 || mbar_test(&bar_s_free[i], (ns - 1) & 1)) &&
+              mbar_test(&bar_k_full[ns % C::NS], (ns / C::NS) & 1)) {
             tc_fence_after();
-            issue_qk<D>(tS[i], sQ + i * C::TILE_BYTES, sK + st1 * C::TILE_BYTES, idesc_s);
+            issue_qk<D>(tmem + C::TM_S + i * BN, sQ + i * C::QTILE, sK + (ns % C::NS) * C::KTILE, idesc_s);
             mma_commit(&bar_s_full[i]);
+            ++ns;
+            progress = true;
+          }
+          if (np < ns && mbar_test(&bar_p_full[i], np & 1) && mbar_test(&bar_v_full[np % C::NS], (np / C::NS) & 1)) {
+            tc_fence_after();
+            issue_pv<D>(tmem + C::TM_O + i * D, tmem + C::TM_P + i * (BN / 2), sV + (np % C::NS) * C::KTILE, np > 0);
+            mma_commit(&bar_o_done[i]);
+            ++np;
+            progress = true;
           }
         }
-        if (!ok) break;
-        mma_commit(&bar_kv_empty[st]);
+        while (released < nmax && (released >= n_0 || next_pv0 > released) && (released >= n_1 || next_pv1 > released)) {
+          mma_commit(&bar_kv_empty[released % C::NS]);
+          ++released;
+        }
+        if (progress) {
+          idle_since = 0;
+        } else {
+          const unsigned long long now = globaltimer_ns();
+          if (idle_since == 0) {
+            idle_since = now;
+          } else if (now - idle_since > kWaitLimitNs || *abort_flag) {
+            if (!*abort_flag) {
+              *abort_flag = 1;
+              atomicOr(ab.status, kStatusWaitTimeout);
+            }
+            ok = false;
+          }
+        }
       }
       // All MMAs must retire before TMEM is released.
       mma_commit(bar_fin);
@@ -222,40 +262,47 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else {
     // ------------------------------------------------------------------ softmax warpgroups
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
     const int i = warp / 4;
     const int t = threadIdx.x % 128;
-    const int row = row0[i] + t;
-    const int n = nblk[i];
+    const int row = (i ? row0_1 : row0_0) + t;
+    const int n = i ? n_1 : n_0;
     const uint32_t lane_off = uint32_t((warp % 4) * 32) << 16;
-    const uint32_t tS = tmem + lane_off + (i ? C::TM_S1 : C::TM_S0);
-    const uint32_t tO = tmem + lane_off + (i ? C::TM_O1 : C::TM_O0);
+    const uint32_t tS = tmem + lane_off + C::TM_S + i * BN;
+    const uint32_t tP = tmem + lane_off + C::TM_P + i * (BN / 2);
+    const uint32_t tO = tmem + lane_off + C::TM_O + i * D;
     const float scale = args.qk_scale;
+    const uint64_t scale2 = f2(scale, scale);
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < n; ++j) {
       if (!warp_wait(&bar_s_full[i], j & 1, ab)) { ok = false; break; }
       tc_fence_after();
-      uint32_t s[128];
-      tmem_load_cols<128>(tS, s);
+      uint32_t s[BN];
+      tmem_load_cols<BN>(tS, s);
       tmem_wait_ld();
-      reg_fence<128>(s);
+      reg_fence<BN>(s);
+      tc_fence_before();
+      mbar_arrive(&bar_s_free[i]);  // the tensor core may now write S(j+1) of this tile
 
-      // Columns past N (ragged tail) and above the diagonal (causal) only occur in the last block.
-      const bool last = (j == n - 1);
-      const int col0 = j * C::BN;
+      // Columns past N (ragged tail) only occur in the last block; columns above the diagonal
+      // (causal) in every block that reaches past the tile's first row (the last BM / BN blocks).
+      const int col0 = j * BN;
+      const bool last = (col0 + BN > N) || (CAUSAL && col0 + BN - 1 > row - t);
       int lim = N - col0;
       if (CAUSAL) lim = min(lim, row - col0 + 1);
-      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
       if (last) {
 #pragma unroll
-        for (int c = 0; c < 128; ++c)
-          mx[c & 3] = fmaxf(mx[c & 3], c < lim ? __uint_as_float(s[c]) : -INFINITY);
-      } else {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) mx[c & 3] = fmaxf(mx[c & 3], __uint_as_float(s[c]));
+        for (int c = 0; c < BN; ++c)
+          if (c >= lim) s[c] = __float_as_uint(-INFINITY);
       }
-      const float m_cand = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale;
-
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN; c += 4) {
+        mx0 = fmax3(mx0, __uint_as_float(s[c]), __uint_as_float(s[c + 1]));
+        mx1 = fmax3(mx1, __uint_as_float(s[c + 2]), __uint_as_float(s[c + 3]));
+      }
+      const float m_cand = fmaxf(mx0, mx1) * scale;
       float alpha = 1.f;
       bool need = false;
       if (j == 0) {
@@ -266,10 +313,42 @@ __global__ void __launch_bounds__(320, 1)
         l_run *= alpha;
         need = true;
       }
-      if (__any_sync(0xffffffffu, need)) {
-        // Rescale this warp's 32 rows of O once the previous PV MMA has landed.
+
+      // P = exp2(S * scale - m): kEmuPairs of every 8 column pairs on the FMA pipe, the rest on MUFU.
+      const uint64_t negm2 = f2(-m_run, -m_run);
+      float ls0 = 0.f, ls1 = 0.f, ls2 = 0.f, ls3 = 0.f;
+      uint32_t p[BN / 2];
+#pragma unroll
+      for (int c = 0; c < BN; c += 2) {
+        const uint64_t x = ffma2(f2(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), scale2, negm2);
+        float2 e;
+        if (((c / 2) & 7) < kEmuPairs) {
+          e = f2_unpack(exp2_poly_x2(x));
+        } else {
+          const float2 xv = f2_unpack(x);
+          e = make_float2(ex2_approx(xv.x), ex2_approx(xv.y));
+        }
+        if (last) {
+          e.x = c < lim ? e.x : 0.f;
+          e.y = c + 1 < lim ? e.y : 0.f;
+        }
+        if ((c / 2) & 1) {
+          ls2 += e.x;
+          ls3 += e.y;
+        } else {
+          ls0 += e.x;
+          ls1 += e.y;
+        }
+        p[c / 2] = pack_half2(e.x, e.y);
+      }
+      l_run += (ls0 + ls1) + (ls2 + ls3);
+
+      // PV(j-1) must have landed before P and O of this tile are touched again.
+      if (j > 0) {
         if (!warp_wait(&bar_o_done[i], (j - 1) & 1, ab)) { ok = false; break; }
         tc_fence_after();
+      }
+      if (__any_sync(0xffffffffu, need)) {
 #pragma unroll
         for (int c0 = 0; c0 < D; c0 += 32) {
           constexpr int W = D < 32 ? D : 32;
@@ -282,29 +361,7 @@ __global__ void __launch_bounds__(320, 1)
           tmem_store_cols<W>(tO + c0, o);
         }
       }
-
-      const float neg_m = -m_run;
-      uint32_t p[64];
-      float ls[4] = {0.f, 0.f, 0.f, 0.f};
-      if (last) {
-#pragma unroll
-        for (int c = 0; c < 128; c += 2) {
-          const float p0 = c < lim ? ex2_approx(fmaf(__uint_as_float(s[c]), scale, neg_m)) : 0.f;
-          const float p1 = c + 1 < lim ? ex2_approx(fmaf(__uint_as_float(s[c + 1]), scale, neg_m)) : 0.f;
-          ls[(c >> 1) & 3] += p0 + p1;
-          p[c >> 1] = pack_half2(p0, p1);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 128; c += 2) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(s[c]), scale, neg_m));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(s[c + 1]), scale, neg_m));
-          ls[(c >> 1) & 3] += p0 + p1;
-          p[c >> 1] = pack_half2(p0, p1);
-        }
-      }
-      l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
-      tmem_store_cols<64>(tS, p);
+      tmem_store_cols<BN / 2>(tP, p);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bar_p_full[i]);
@@ -354,11 +411,21 @@ cudaError_t launch_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUte
   const long long grid = (long long)nct * a.Z * a.H;
   if (grid <= 0) return cudaSuccess;
   if (grid > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-  kern<<<dim3((unsigned)grid), dim3(320), C::SMEM_BYTES, s>>>(tq, tk, tv, a);
+  kern<<<dim3((unsigned)grid), dim3(384), C::SMEM_BYTES, s>>>(tq, tk, tv, a);
   return cudaGetLastError();
 }
 
 }  // namespace
+
+int fwd_f16_kv_rows(int D) {
+  switch (D) {
+    case 16: return FwdCfg<16>::BN;
+    case 32: return FwdCfg<32>::BN;
+    case 64: return FwdCfg<64>::BN;
+    case 128: return FwdCfg<128>::BN;
+    default: return 0;
+  }
+}
 
 cudaError_t launch_fwd_f16(int D, bool causal, int tile_cfg, const CUtensorMap& tq, const CUtensorMap& tk,
                            const CUtensorMap& tv, const FwdArgs& a, cudaStream_t s) {
