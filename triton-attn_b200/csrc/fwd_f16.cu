@@ -9,14 +9,16 @@
 //   warpgroup 0 (warps 0-3)   softmax for query tile 0 (thread t owns TMEM lane t = query row t)
 //   warpgroup 1 (warps 4-7)   softmax for query tile 1
 //   warpgroup 2: warp 8       TMA producer (Q tiles once, then K/V blocks through an NS-stage ring)
-//                warp 9       TMEM allocator + MMA issuer (one thread, event loop)
-//                warps 10-11  idle (they complete the warpgroup for the register split)
-// setmaxnreg moves registers from warpgroup 2 (48 per thread) to the softmax warpgroups (224), so a
+//                warps 9, 10  MMA issuers for tile 0 and tile 1 (one elected lane issues)
+//                warp 11      TMEM allocator
+// setmaxnreg moves registers from warpgroup 2 (56 per thread) to the softmax warpgroups (216), so a
 // softmax thread keeps its whole score row in registers and reads S from TMEM once.
 // TMEM (512 columns): S0, S1 [BN each] | P0, P1 [BN/2 each, fp16 pairs] | O0, O1 [D each]. P has its own
 // buffer, so the tensor core computes S(j+1) of a tile while that tile's softmax still exponentiates
-// S(j): as soon as a softmax warpgroup has S(j) in registers it releases the S buffer (s_free), and
-// the MMA issuer starts the next QK^T. P then feeds the PV MMA as the A operand straight from TMEM.
+// S(j): as soon as a softmax warpgroup has S(j) in registers it releases the S buffer (s_free) and
+// its tile's issuer starts the next QK^T. P then feeds the PV MMA as the A operand straight from
+// TMEM. The two warpgroups ping-pong on the exponent pass (the MUFU-bound part) through a token pair
+// of mbarriers.
 // The running max is rescaled lazily: O (in TMEM) and l are only corrected when a row's max grows by
 // more than kRescaleThreshold (log2 units); P values stay below 2^kRescaleThreshold, exact in fp16.
 #include "common.cuh"
@@ -30,9 +32,9 @@ constexpr float kRescaleThreshold = 8.0f;
 // on MUFU (16 results/clk/SM), whose rate alone caps the D = 64 forward near half the tensor rate.
 constexpr int kEmuPairs = 0;
 // Register split (setmaxnreg): launch = 384 threads x 168 registers = 64512; softmax warpgroups take
-// 224 and warpgroup 2 keeps 48: 8*32*224 + 4*32*48 = 63488 <= 64512.
-constexpr int kSoftmaxRegs = 224;
-constexpr int kProducerRegs = 48;
+// 216 and warpgroup 2 keeps 56: 8*32*216 + 4*32*56 = 62464 <= 64512.
+constexpr int kSoftmaxRegs = 216;
+constexpr int kProducerRegs = 56;
 
 template <int D>
 struct FwdCfg {
@@ -51,8 +53,9 @@ struct FwdCfg {
   static constexpr int OFF_K = 2 * QTILE;
   static constexpr int OFF_V = OFF_K + NS * KTILE;
   static constexpr int OFF_BAR = OFF_V + NS * KTILE;
-  // q_full, k_full[NS], v_full[NS], kv_empty[NS], s_full[2], s_free[2], p_full[2], o_done[2], fin
-  static constexpr int NBARS = 1 + 3 * NS + 9;
+  // q_full, k_full[NS], v_full[NS], kv_empty[2][NS], s_full[2], o_done[2], exp_done[2], fin[2],
+  // s_free[2], p_full[2]
+  static constexpr int NBARS = 1 + 4 * NS + 12;
   static constexpr int OFF_MISC = OFF_BAR + NBARS * 8;  // tmem base (u32), abort flag (int)
   static constexpr int SMEM_USED = OFF_MISC + 16;
   // Request at least ~116 KB so exactly one CTA (which owns all 512 TMEM columns) fits per SM.
@@ -65,38 +68,97 @@ struct FwdCfg {
   static constexpr uint32_t IDESC_PV = idesc_f16_f32(128, D, true);
 };
 
-template <int D>
-__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_base, uint32_t k_base, uint32_t idesc) {
+// S_i = Q_i K^T for the K block in ring stage ST: D/16 MMAs (K = 16 each). All descriptor offsets are
+// compile-time constants added to loop-invariant base descriptors.
+template <int D, int ST>
+__device__ __forceinline__ void issue_qk_st(int i, uint32_t d_tmem, uint64_t dQ, uint64_t dK, uint32_t idesc) {
   using C = FwdCfg<D>;
+  // Opaque copies: keep the compiler from hoisting every stage's descriptors into registers.
+  asm volatile("" : "+l"(dQ), "+l"(dK));
+  const uint64_t a0 = i ? dQ + uint64_t(C::QTILE >> 4) : dQ;
 #pragma unroll
   for (int kk = 0; kk < D / 16; ++kk) {
-    const uint32_t col = kk * 16 / C::CW, inner = ((kk * 16) % C::CW) * 2;
-    const uint64_t a = smem_desc(q_base + col * C::QCHUNK + inner, 16, 8 * C::SWB, C::LAYOUT);
-    const uint64_t b = smem_desc(k_base + col * C::KCHUNK + inner, 16, 8 * C::SWB, C::LAYOUT);
-    mma_f16_ss(d_tmem, a, b, idesc, kk > 0 ? 1u : 0u);
+    const int col = kk * 16 / C::CW, inner = ((kk * 16) % C::CW) * 2;
+    mma_f16_ss_elect(d_tmem, a0 + uint64_t((col * C::QCHUNK + inner) >> 4),
+                     dK + uint64_t((ST * C::KTILE + col * C::KCHUNK + inner) >> 4), idesc, kk > 0 ? 1u : 0u);
   }
 }
-
 template <int D>
-__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_base, bool accumulate) {
-  using C = FwdCfg<D>;
-#pragma unroll
-  for (int kk = 0; kk < C::BN / 16; ++kk) {
-    const uint64_t b = smem_desc(v_base + kk * 16 * C::SWB, C::KCHUNK, 8 * C::SWB, C::LAYOUT);
-    mma_f16_ts(d_tmem, p_tmem + kk * 8, b, C::IDESC_PV, (accumulate || kk > 0) ? 1u : 0u);
+__device__ __forceinline__ void issue_qk_stage(int st, int i, uint32_t d_tmem, uint64_t dQ, uint64_t dK,
+                                               uint32_t idesc) {
+  static_assert(FwdCfg<D>::NS == 4, "stage dispatch");
+  switch (st) {
+    case 0: issue_qk_st<D, 0>(i, d_tmem, dQ, dK, idesc); break;
+    case 1: issue_qk_st<D, 1>(i, d_tmem, dQ, dK, idesc); break;
+    case 2: issue_qk_st<D, 2>(i, d_tmem, dQ, dK, idesc); break;
+    default: issue_qk_st<D, 3>(i, d_tmem, dQ, dK, idesc); break;
   }
 }
 
-__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
+// O_i += P_i V for the V block in ring stage ST: BN/16 MMAs with P (fp16) read from TMEM.
+template <int D, int ST>
+__device__ __forceinline__ void issue_pv_st(uint32_t d_tmem, uint32_t p_tmem, uint64_t dV, uint32_t accumulate) {
+  using C = FwdCfg<D>;
+  asm volatile("" : "+l"(dV));
+#pragma unroll
+  for (int kk = 0; kk < C::BN / 16; ++kk)
+    mma_f16_ts_elect(d_tmem, p_tmem + kk * 8, dV + uint64_t((ST * C::KTILE + kk * 16 * C::SWB) >> 4), C::IDESC_PV,
+                     kk > 0 ? 1u : accumulate);
+}
+template <int D>
+__device__ __forceinline__ void issue_pv_stage(int st, uint32_t d_tmem, uint32_t p_tmem, uint64_t dV,
+                                               uint32_t accumulate) {
+  switch (st) {
+    case 0: issue_pv_st<D, 0>(d_tmem, p_tmem, dV, accumulate); break;
+    case 1: issue_pv_st<D, 1>(d_tmem, p_tmem, dV, accumulate); break;
+    case 2: issue_pv_st<D, 2>(d_tmem, p_tmem, dV, accumulate); break;
+    default: issue_pv_st<D, 3>(d_tmem, p_tmem, dV, accumulate); break;
+  }
+}
+
+// Max of one row of raw scores; MASK ignores columns >= lim.
+template <int BN, bool MASK>
+__device__ __forceinline__ float row_max(const uint32_t* s, int lim) {
+  float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+  for (int c = 0; c < BN; c += 2) {
+    float a = __uint_as_float(s[c]), b = __uint_as_float(s[c + 1]);
+    if (MASK) {
+      a = c < lim ? a : -INFINITY;
+      b = c + 1 < lim ? b : -INFINITY;
+    }
+    m[(c / 2) & 3] = fmax3(m[(c / 2) & 3], a, b);
+  }
+  return fmax3(fmaxf(m[0], m[1]), m[2], m[3]);
+}
+
+// One row of P = exp2(S * scale - m) as fp16 pairs (p[c/2] = columns c, c+1) and its fp32 sum.
+// kEmuPairs of every 8 column pairs use the FMA-pipe exp2, the rest MUFU. MASK zeroes columns >= lim.
+template <int BN, bool MASK>
+__device__ __forceinline__ float exp_row(const uint32_t* s, uint32_t* p, uint64_t scale2, uint64_t negm2, int lim) {
+  uint64_t acc0 = 0, acc1 = 0;
+#pragma unroll
+  for (int c = 0; c < BN; c += 2) {
+    const uint64_t x = ffma2(f2(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), scale2, negm2);
+    float2 e;
+    if (((c / 2) & 7) < kEmuPairs) {
+      e = f2_unpack(exp2_poly_x2(x));
+    } else {
+      const float2 xv = f2_unpack(x);
+      e = make_float2(ex2_approx(xv.x), ex2_approx(xv.y));
+    }
+    if (MASK) {
+      e.x = c < lim ? e.x : 0.f;
+      e.y = c + 1 < lim ? e.y : 0.f;
+    }
+    if ((c / 2) & 1)
+      acc1 = fadd2(acc1, f2(e.x, e.y));
+    else
+      acc0 = fadd2(acc0, f2(e.x, e.y));
+    p[c / 2] = pack_half2(e.x, e.y);
+  }
+  const float2 t = f2_unpack(fadd2(acc0, acc1));
+  return t.x + t.y;
 }
 
 template <int D, bool CAUSAL>
@@ -112,14 +174,15 @@ __global__ void __launch_bounds__(384, 1)
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* bar_q = bars;
-  uint64_t* bar_k_full = bars + 1;
-  uint64_t* bar_v_full = bars + 1 + C::NS;
-  uint64_t* bar_kv_empty = bars + 1 + 2 * C::NS;
-  uint64_t* bar_s_full = bars + 1 + 3 * C::NS;
-  uint64_t* bar_s_free = bar_s_full + 2;
-  uint64_t* bar_p_full = bar_s_full + 4;
-  uint64_t* bar_o_done = bar_s_full + 6;
-  uint64_t* bar_fin = bar_s_full + 8;
+  uint64_t* bar_k_full = bars + 1;                   // [NS]
+  uint64_t* bar_v_full = bars + 1 + C::NS;           // [NS]
+  uint64_t* bar_kv_empty = bars + 1 + 2 * C::NS;     // [2][NS]: tile i is done with the block in stage s
+  uint64_t* bar_s_full = bars + 1 + 4 * C::NS;       // [2]
+  uint64_t* bar_o_done = bar_s_full + 2;             // [2]
+  uint64_t* bar_exp_done = bar_s_full + 4;           // [2]: warpgroup i finished the exponent pass
+  uint64_t* bar_fin = bar_s_full + 6;                // [2]
+  uint64_t* bar_s_free = bar_s_full + 8;             // [2]: the tile's softmax holds S(j) in registers
+  uint64_t* bar_p_full = bar_s_full + 10;            // [2]: the tile's softmax has stored P(j)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
   const CtaAbort ab{abort_flag, args.status};
@@ -149,18 +212,20 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(&bar_k_full[s], 1);
       mbar_init(&bar_v_full[s], 1);
       mbar_init(&bar_kv_empty[s], 1);
+      mbar_init(&bar_kv_empty[C::NS + s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar_s_full[i], 1);
+      mbar_init(&bar_o_done[i], 1);
+      mbar_init(&bar_exp_done[i], 128);
+      mbar_init(&bar_fin[i], 1);
       mbar_init(&bar_s_free[i], 128);
       mbar_init(&bar_p_full[i], 128);
-      mbar_init(&bar_o_done[i], 1);
     }
-    mbar_init(bar_fin, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 9) {
+  if (warp == 11) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -188,9 +253,16 @@ __global__ void __launch_bounds__(384, 1)
           tma_load_4d(sQ + i * C::QTILE + ch * C::QCHUNK, &tm_q, ch * C::CW, i ? row0_1 : row0_0, hi, zi, bar_q);
       }
       int j = 0;
-      for (; j < nmax; ++j) {
+      bool ok = true;
+      for (; ok && j < nmax; ++j) {
         const int st = j % C::NS;
-        if (j >= C::NS && !mbar_wait(&bar_kv_empty[st], ((j / C::NS) - 1) & 1, ab)) break;
+        if (j >= C::NS) {  // both tiles that used the stage's previous block must be done with it
+          const int old = j - C::NS;
+          for (int i = 0; i < 2 && ok; ++i)
+            if (old < (i ? n_1 : n_0) && !mbar_wait(&bar_kv_empty[i * C::NS + st], ((j / C::NS) - 1) & 1, ab))
+              ok = false;
+          if (!ok) break;
+        }
         mbar_arrive_expect_tx(&bar_k_full[st], C::KTILE);
         for (int ch = 0; ch < C::NCH; ++ch)
           tma_load_4d(sK + st * C::KTILE + ch * C::KCHUNK, &tm_k, ch * C::CW, j * BN, hi, zi, &bar_k_full[st]);
@@ -205,60 +277,48 @@ __global__ void __launch_bounds__(384, 1)
         mbar_drain(&bar_k_full[jj % C::NS], (jj / C::NS) & 1, lim);
         mbar_drain(&bar_v_full[jj % C::NS], (jj / C::NS) & 1, lim);
       }
-    } else if (warp == 9 && lane == 0) {
-      // -------------------------------------------------------------- MMA issuer (event loop)
-      // Per tile: S(b) needs the tile's S buffer released (s_free of b-1) and K(b); PV(b) needs P(b)
-      // (p_full of b) and V(b). Whatever is ready is issued; a K/V stage is released once every tile
-      // that uses block b has issued PV(b).
+    } else if (warp == 9 || warp == 10) {
+      // -------------------------------------------------------------- MMA issuer of tile i
+      // Order within a tile = the order its softmax releases inputs: S(j+1) once the softmax holds
+      // S(j) in registers (s_free), then PV(j) once it has stored P(j) (p_full). The whole warp runs
+      // the loop; elect.sync inside each MMA picks the issuing lane, and every descriptor is a
+      // loop-invariant base plus a compile-time constant, so the MMAs go out at tensor-core rate.
+      const int i = warp - 9;
+      const int n = i ? n_1 : n_0;
       const uint32_t idesc_s = C::IDESC_S | (args.negate_s ? (1u << 13) : 0u);
-      bool ok = mbar_wait(bar_q, 0, ab);
-      int next_s0 = 0, next_s1 = 0, next_pv0 = 0, next_pv1 = 0, released = 0;
-      unsigned long long idle_since = 0;
-      while (ok && (next_pv0 < n_0 || next_pv1 < n_1)) {
-        bool progress = false;
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const int n = i ? n_1 : n_0;
-          int& ns = i ? next_s1 : next_s0;
-          int& np = i ? next_pv1 : next_pv0;
-          if (ns < n && (ns == 0 || mbar_test(&bar_s_free[i], (ns - 1) & 1)) &&
-              mbar_test(&bar_k_full[ns % C::NS], (ns / C::NS) & 1)) {
-            tc_fence_after();
-            issue_qk<D>(tmem + C::TM_S + i * BN, sQ + i * C::QTILE, sK + (ns % C::NS) * C::KTILE, idesc_s);
-            mma_commit(&bar_s_full[i]);
-            ++ns;
-            progress = true;
-          }
-          if (np < ns && mbar_test(&bar_p_full[i], np & 1) && mbar_test(&bar_v_full[np % C::NS], (np / C::NS) & 1)) {
-            tc_fence_after();
-            issue_pv<D>(tmem + C::TM_O + i * D, tmem + C::TM_P + i * (BN / 2), sV + (np % C::NS) * C::KTILE, np > 0);
-            mma_commit(&bar_o_done[i]);
-            ++np;
-            progress = true;
-          }
-        }
-        while (released < nmax && (released >= n_0 || next_pv0 > released) && (released >= n_1 || next_pv1 > released)) {
-          mma_commit(&bar_kv_empty[released % C::NS]);
-          ++released;
-        }
-        if (progress) {
-          idle_since = 0;
-        } else {
-          const unsigned long long now = globaltimer_ns();
-          if (idle_since == 0) {
-            idle_since = now;
-          } else if (now - idle_since > kWaitLimitNs || *abort_flag) {
-            if (!*abort_flag) {
-              *abort_flag = 1;
-              atomicOr(ab.status, kStatusWaitTimeout);
-            }
-            ok = false;
-          }
-        }
+      const uint64_t dQ = smem_desc(sQ, 16, 8 * C::SWB, C::LAYOUT);
+      const uint64_t dK = smem_desc(sK, 16, 8 * C::SWB, C::LAYOUT);
+      const uint64_t dV = smem_desc(sV, C::KCHUNK, 8 * C::SWB, C::LAYOUT);
+      const uint32_t tS = tmem + C::TM_S + i * BN, tP = tmem + C::TM_P + i * (BN / 2), tO = tmem + C::TM_O + i * D;
+      bool ok = n > 0 && warp_wait(bar_q, 0, ab) && warp_wait(&bar_k_full[0], 0, ab);
+      if (ok) {
+        tc_fence_after();
+        issue_qk_stage<D>(0, i, tS, dQ, dK, idesc_s);
+        mma_commit_elect(&bar_s_full[i]);
       }
-      // All MMAs must retire before TMEM is released.
-      mma_commit(bar_fin);
-      mbar_drain(bar_fin, 0, 100ull * 1000ull * 1000ull);
+      for (int j = 0; ok && j < n; ++j) {
+        if (j + 1 < n) {
+          const int b = j + 1;
+          if (!warp_wait(&bar_s_free[i], j & 1, ab) || !warp_wait(&bar_k_full[b % C::NS], (b / C::NS) & 1, ab)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_qk_stage<D>(b % C::NS, i, tS, dQ, dK, idesc_s);
+          mma_commit_elect(&bar_s_full[i]);
+        }
+        if (!warp_wait(&bar_p_full[i], j & 1, ab) || !warp_wait(&bar_v_full[j % C::NS], (j / C::NS) & 1, ab)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_pv_stage<D>(j % C::NS, tO, tP, dV, j > 0 ? 1u : 0u);
+        mma_commit_elect(&bar_o_done[i]);
+        mma_commit_elect(&bar_kv_empty[i * C::NS + j % C::NS]);
+      }
+      // Every MMA of this tile must retire before TMEM is released.
+      mma_commit_elect(&bar_fin[i]);
+      mbar_drain(&bar_fin[i], 0, 100ull * 1000ull * 1000ull);
     }
   } else {
     // ------------------------------------------------------------------ softmax warpgroups
@@ -291,18 +351,7 @@ __global__ void __launch_bounds__(384, 1)
       const bool last = (col0 + BN > N) || (CAUSAL && col0 + BN - 1 > row - t);
       int lim = N - col0;
       if (CAUSAL) lim = min(lim, row - col0 + 1);
-      if (last) {
-#pragma unroll
-        for (int c = 0; c < BN; ++c)
-          if (c >= lim) s[c] = __float_as_uint(-INFINITY);
-      }
-      float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < BN; c += 4) {
-        mx0 = fmax3(mx0, __uint_as_float(s[c]), __uint_as_float(s[c + 1]));
-        mx1 = fmax3(mx1, __uint_as_float(s[c + 2]), __uint_as_float(s[c + 3]));
-      }
-      const float m_cand = fmaxf(mx0, mx1) * scale;
+      const float m_cand = (last ? row_max<BN, true>(s, lim) : row_max<BN, false>(s, lim)) * scale;
       float alpha = 1.f;
       bool need = false;
       if (j == 0) {
@@ -314,34 +363,19 @@ __global__ void __launch_bounds__(384, 1)
         need = true;
       }
 
-      // P = exp2(S * scale - m): kEmuPairs of every 8 column pairs on the FMA pipe, the rest on MUFU.
-      const uint64_t negm2 = f2(-m_run, -m_run);
-      float ls0 = 0.f, ls1 = 0.f, ls2 = 0.f, ls3 = 0.f;
-      uint32_t p[BN / 2];
-#pragma unroll
-      for (int c = 0; c < BN; c += 2) {
-        const uint64_t x = ffma2(f2(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), scale2, negm2);
-        float2 e;
-        if (((c / 2) & 7) < kEmuPairs) {
-          e = f2_unpack(exp2_poly_x2(x));
-        } else {
-          const float2 xv = f2_unpack(x);
-          e = make_float2(ex2_approx(xv.x), ex2_approx(xv.y));
-        }
-        if (last) {
-          e.x = c < lim ? e.x : 0.f;
-          e.y = c + 1 < lim ? e.y : 0.f;
-        }
-        if ((c / 2) & 1) {
-          ls2 += e.x;
-          ls3 += e.y;
-        } else {
-          ls0 += e.x;
-          ls1 += e.y;
-        }
-        p[c / 2] = pack_half2(e.x, e.y);
+      // Ping-pong: the two warpgroups take turns on the exponent pass (the MUFU-bound part), so one
+      // exponentiates while the other loads S, reduces the max and stores P. Order: tile 0 block j,
+      // tile 1 block j, tile 0 block j+1, ...; a turn is only awaited if the other tile has that block.
+      const int other_n = i ? n_0 : n_1;
+      if (i == 1 ? (j < other_n) : (j >= 1 && j - 1 < other_n)) {
+        if (!warp_wait(&bar_exp_done[1 - i], (i == 1 ? j : j - 1) & 1, ab)) { ok = false; break; }
       }
-      l_run += (ls0 + ls1) + (ls2 + ls3);
+      // P = exp2(S * scale - m); the masked variant only runs for blocks that need it, so the column
+      // tests never cost the unmasked blocks anything.
+      uint32_t p[BN / 2];
+      l_run += last ? exp_row<BN, true>(s, p, scale2, f2(-m_run, -m_run), lim)
+                    : exp_row<BN, false>(s, p, scale2, f2(-m_run, -m_run), lim);
+      mbar_arrive(&bar_exp_done[i]);
 
       // PV(j-1) must have landed before P and O of this tile are touched again.
       if (j > 0) {
@@ -394,7 +428,7 @@ __global__ void __launch_bounds__(384, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == 11) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
