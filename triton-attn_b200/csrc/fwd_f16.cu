@@ -30,7 +30,7 @@ namespace {
 constexpr float kRescaleThreshold = 8.0f;
 // Of every 8 column pairs of a row, this many take exp2 on the FMA pipe (exp2_poly_x2) and the rest
 // on MUFU (16 results/clk/SM), whose rate alone caps the D = 64 forward near half the tensor rate.
-constexpr int kEmuPairs = 0;
+constexpr int kEmuPairs = 2;
 // Register split (setmaxnreg): launch = 384 threads x 168 registers = 64512; softmax warpgroups take
 // 216 and warpgroup 2 keeps 56: 8*32*216 + 4*32*56 = 62464 <= 64512.
 constexpr int kSoftmaxRegs = 216;
