@@ -242,7 +242,7 @@ int bwd_common(bool dq_pass, const void* q, const void* k, const void* v, const 
   CUtensorMap tq, tk, tv, tdo;
   // dQ: query tiles of 128 rows, key blocks of 64 rows; dK/dV: key tiles of 128 rows, query blocks of 64.
   int q_rows = 0, kv_rows = 0;
-  bwd_f16_box_rows(dq_pass, &q_rows, &kv_rows);  // must match the kernels' shared-memory slots
+  bwd_f16_box_rows(D, dq_pass, &q_rows, &kv_rows);  // must match the kernels' shared-memory slots
   if ((rc = encode_f16(&tq, q, a.sq, Z, H, N, D, q_rows)) != TATTN_OK) return rc;
   if ((rc = encode_f16(&tk, k, a.sk, Z, H, N, D, kv_rows)) != TATTN_OK) return rc;
   if ((rc = encode_f16(&tv, v, a.sv, Z, H, N, D, kv_rows)) != TATTN_OK) return rc;

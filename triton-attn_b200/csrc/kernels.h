@@ -41,8 +41,9 @@ struct BwdArgs {
 // Rows per K/V block of the fp16 forward for head dim D: the TMA box height of its K and V tensor maps
 // (the Q map always uses 128-row boxes). The kernel's shared-memory slots are sized for exactly this.
 int fwd_f16_kv_rows(int D);
-// TMA box heights of the fp16 backward kernels' Q/dO and K/V tensor maps (dQ pass or dK/dV pass).
-void bwd_f16_box_rows(bool dq_pass, int* q_rows, int* kv_rows);
+// TMA box heights of the fp16 backward kernels' Q/dO and K/V tensor maps for head dim D (dQ pass or
+// dK/dV pass).
+void bwd_f16_box_rows(int D, bool dq_pass, int* q_rows, int* kv_rows);
 
 // fp16 tcgen05 kernels (tensor maps describe [Z, H, N, D] tensors as 4-D {D, N, H, Z}).
 cudaError_t launch_fwd_f16(int D, bool causal, int tile_cfg, const CUtensorMap& tq, const CUtensorMap& tk,
