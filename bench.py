@@ -41,6 +41,9 @@ CONFIGS = {
 }
 T4_PUBLISHED = {"cfg2": 16.9, "cfg3": 15.9}  # reference fwd+bwd TFLOP/s on a T4
 L2_BYTES = 126 * 2**20
+# DRAM bytes (read + write) of one launch of the dominant kernel, from the committed ncu capture
+# profiles/bwd_dkdv_cfg2.md (dram__bytes_read.sum + dram__bytes_write.sum); None for other configs.
+NCU_TRAFFIC = {("cfg2", "dkdv"): 136_381_440 + 41_013_248}
 
 
 def flops(b: int, h: int, n: int, d: int, causal: bool, mode: str) -> float:
@@ -80,7 +83,7 @@ def peaks() -> dict:
 
 # ------------------------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clock / throttle samples every 200 ms while the timed region runs."""
+    """nvidia-smi clock / throttle samples every 50 ms while the timed region runs."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -95,7 +98,7 @@ class ClockSampler:
     def __enter__(self) -> ClockSampler:
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
                  "-i", str(self.gpu)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
             )  # fmt: skip
@@ -144,22 +147,26 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------------------- CPU
-def _cpu_worker(args: tuple) -> float:
-    """Time the oracle's tiled forward+backward on (b, h) pairs [lo, hi) with bounded block counts."""
+def _cpu_worker(args: tuple) -> tuple:
+    """Time the oracle's tiled forward+backward on (b, h) pairs [lo, hi), once with `blocks` and once
+    with 2*`blocks` outer blocks: (fwd_1, bwd_1, fwd_2, bwd_2) seconds."""
     import numpy as np
 
     from oracle import tiled_backward, tiled_forward
 
-    (b_h, n, d, causal, lo, hi, row_blocks, col_blocks, seed) = args
+    (b_h, n, d, causal, lo, hi, blocks, seed) = args
     rng = np.random.default_rng(seed + lo)
     shape = (hi - lo, n, d)
     q, k, v, do = (rng.standard_normal(shape).astype(np.float16) for _ in range(4))
-    t0 = time.perf_counter()
-    o, m = tiled_forward(q, k, v, causal, row_blocks=row_blocks)
-    t1 = time.perf_counter()
-    tiled_backward(q, k, v, o, m, do, causal, col_blocks=col_blocks)
-    t2 = time.perf_counter()
-    return t1 - t0, t2 - t1
+    out = []
+    for nb in (blocks, 2 * blocks):
+        t0 = time.perf_counter()
+        o, m = tiled_forward(q, k, v, causal, row_blocks=nb)
+        t1 = time.perf_counter()
+        tiled_backward(q, k, v, o, m, do, causal, col_blocks=nb)
+        t2 = time.perf_counter()
+        out += [t1 - t0, t2 - t1]
+    return tuple(out)
 
 
 def _pair_fraction(nb: int, taken: int, causal: bool, reverse: bool) -> float:
@@ -171,32 +178,59 @@ def _pair_fraction(nb: int, taken: int, causal: bool, reverse: bool) -> float:
     return sum(w[:taken]) / sum(w)
 
 
-def cpu_baseline(cfg: str, budget_s: float, workers: int) -> dict:
+def cpu_pool(cfg: str, workers: int):
+    """A pool of `workers` spawned processes for cpu_baseline (spawned, so it is safe after CUDA init)."""
+    b, h = CONFIGS[cfg][:2]
+    return mp.get_context("spawn").Pool(max(1, min(workers, b * h)))
+
+
+def _extrapolate(t1: float, t2: float, f1: float, f2: float) -> float:
+    """Full-loop time from samples t1, t2 covering loop fractions f1 < f2 of the block-pair loop:
+    t = setup + W * f, so W = (t2 - t1) / (f2 - f1) and full = setup + W (setup >= 0)."""
+    w = max(t2 - t1, 0.0) / max(f2 - f1, 1e-9)
+    return max(t1 - w * f1, 0.0) + w
+
+
+def cpu_baseline(cfg: str, budget_s: float, workers: int, pool=None, blocks: int | None = None) -> dict:
     """The reference's CPU path (oracle restatement of reference.py's 16x16-block tiled forward and
     backward, fp16 inputs upcast to fp32) on a bounded sample of the workload, in `workers` spawned
-    processes that split the (batch, head) pairs. Returns TFLOP/s extrapolated to the full workload."""
+    processes that split the (batch, head) pairs. Each worker times the first `blocks` and the first
+    2*`blocks` outer blocks; the difference gives the per-block cost without the fixed setup (fp32
+    copies, delta, output buffers), and the full-workload time is setup + the whole block loop.
+    Returns TFLOP/s for the full workload."""
     b, h, n, d, causal = CONFIGS[cfg]
     pairs = b * h
     nb = (n + 15) // 16
-    # Probe one block to size the sample so the whole measurement takes about `budget_s`.
     workers = max(1, min(workers, pairs))
-    ctx = mp.get_context("spawn")
     bounds = [(pairs * i // workers, pairs * (i + 1) // workers) for i in range(workers)]
-    with ctx.Pool(workers) as pool:
-        probe = pool.map(_cpu_worker, [(pairs, n, d, causal, lo, hi, 1, 1, 0) for lo, hi in bounds])
-        per_blk = max(f + bw for f, bw in probe)
-        take = max(1, min(nb, int(budget_s / max(per_blk, 1e-3))))
-        res = pool.map(_cpu_worker, [(pairs, n, d, causal, lo, hi, take, take, 0) for lo, hi in bounds])
-    t_fwd = max(r[0] for r in res) / _pair_fraction(nb, take, causal, False)
-    t_bwd = max(r[1] for r in res) / _pair_fraction(nb, take, causal, True)
+    own = pool is None
+    if own:
+        pool = cpu_pool(cfg, workers)
+    try:
+        if blocks is None:  # size the sample from a one-block probe so it takes about budget_s
+            probe = pool.map(_cpu_worker, [(pairs, n, d, causal, lo, hi, 1, 0) for lo, hi in bounds])
+            per_blk = max((r[2] + r[3]) / 2 for r in probe)  # upper bound: setup included
+            blocks = max(1, min(nb // 2, int(budget_s / (3 * per_blk))))
+        res = pool.map(_cpu_worker, [(pairs, n, d, causal, lo, hi, blocks, 0) for lo, hi in bounds])
+    finally:
+        if own:
+            pool.close()
+            pool.join()
+    take = blocks
+    ff = [_pair_fraction(nb, take, causal, False), _pair_fraction(nb, 2 * take, causal, False)]
+    fb = [_pair_fraction(nb, take, causal, True), _pair_fraction(nb, 2 * take, causal, True)]
+    t_fwd = max(_extrapolate(r[0], r[2], *ff) for r in res)
+    t_bwd = max(_extrapolate(r[1], r[3], *fb) for r in res)
     total = flops(b, h, n, d, causal, "fwd+bwd")
     return {
         "value": total / (t_fwd + t_bwd) / 1e12,
         "unit": "TFLOP/s",
         "cores": workers,
         "kind": "port",
-        "sample": (f"{cfg} all {pairs} (b,h) pairs, first {take} of {nb} 16-row query blocks (fwd) and "
-                   f"key blocks (bwd); time scaled by block-pair count"),  # fmt: skip
+        "sample": (f"{cfg} all {pairs} (b,h) pairs, first {take} and first {2 * take} of {nb} 16-row "
+                   f"query blocks (fwd) and key blocks (bwd); full time = setup + per-block cost x "
+                   f"block-pair count"),  # fmt: skip
+        "blocks": take,
         "fwd_s_extrapolated": t_fwd,
         "bwd_s_extrapolated": t_bwd,
     }
@@ -394,7 +428,8 @@ def run_gpu(args) -> None:
                 "peak": pk["tflops"],
                 "unit": "TFLOP/s",
                 "frac": round(achieved / pk["tflops"], 4),
-                "traffic": None,
+                "traffic": NCU_TRAFFIC.get((args.config, dom)),
+                "traffic_source": "ncu capture (profiles/bwd_dkdv_cfg2.md)" if (args.config, dom) in NCU_TRAFFIC else None,
                 "flops_per_launch": kflops[dom],
             },
             "e2e": {
@@ -424,12 +459,17 @@ def run_reference(args) -> None:
         return
     cores = max(1, os.cpu_count() or 1)
     vals = []
-    for _ in range(args.warmup):
-        cpu_baseline(args.config, 2.0, cores)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        vals.append(cpu_baseline(args.config, args.cpu_budget / max(1, args.steps), cores))
-    wall = time.perf_counter() - t0
+    # Each step is one bounded sample of the same size (blocks sized once, from the first warm-up
+    # step, so that all steps together cost about cpu_budget seconds).
+    per_step = args.cpu_budget / max(1, args.steps)
+    with cpu_pool(args.config, cores) as pool:
+        first = cpu_baseline(args.config, per_step, cores, pool)
+        for _ in range(args.warmup - 1):
+            cpu_baseline(args.config, per_step, cores, pool, blocks=first["blocks"])
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            vals.append(cpu_baseline(args.config, per_step, cores, pool, blocks=first["blocks"]))
+        wall = time.perf_counter() - t0
     b, h, n, d, causal = CONFIGS[args.config]
     value = statistics.median(v["value"] for v in vals)
     cb = dict(vals[-1])
@@ -460,7 +500,7 @@ def run_reference(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg2")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")

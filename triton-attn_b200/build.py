@@ -64,18 +64,24 @@ def build(force: bool = False, jobs: int = 0, verbose: bool = False) -> str:
         p = subprocess.run(cmd, capture_output=True, text=True)
         if p.returncode != 0:
             raise RuntimeError(f"nvcc failed for {src}:\n{' '.join(cmd)}\n{p.stdout}\n{p.stderr}")
+        with open(obj[:-2] + ".ptxas.log", "w") as f:  # per source, so ptxas.log covers every object
+            f.write(p.stdout + p.stderr)
         return obj, p.stdout + p.stderr
 
     workers = jobs or min(len(sources), os.cpu_count() or 1)
     with ThreadPoolExecutor(max_workers=max(1, workers)) as ex:
         results = list(ex.map(compile_one, sources))
     objs = [o for o, _ in results]
-    logs = "".join(log for _, log in results if log)
-    if logs:
-        with open(os.path.join(BUILD, "ptxas.log"), "w") as f:
-            f.write(logs)
-        if verbose:
-            print(logs)
+    logs = ""
+    for o in objs:
+        lp = o[:-2] + ".ptxas.log"
+        if os.path.exists(lp):
+            with open(lp) as f:
+                logs += f.read()
+    with open(os.path.join(BUILD, "ptxas.log"), "w") as f:
+        f.write(logs)
+    if verbose and logs:
+        print(logs)
     if force or _stale(LIB, objs):
         exports = os.path.join(BUILD, "exports.map")
         with open(exports, "w") as f:
