@@ -103,10 +103,10 @@ __device__ __forceinline__ float2 exp2_pair(uint64_t x) {
   const float2 v = f2_unpack(x);
   return make_float2(ex2_approx(v.x), ex2_approx(v.y));
 }
-// Of every 8 column pairs, this many take exp2 on the FMA pipe (per kernel: the dK/dV compute has
-// more other FMA/ALU work per element).
+// Of every 8 column pairs, this many take exp2 on the FMA pipe (measured per kernel: the dK/dV compute
+// phase, with its M/delta loads and second fp16 pack, is issue-bound and fastest all on MUFU).
 constexpr int kDqEmuPairs = 2;
-constexpr int kDkvEmuPairs = 2;
+constexpr int kDkvEmuPairs = 0;
 
 // Write a [128, D] fp32 TMEM accumulator slice (this thread's lane, columns [c_begin, c_begin + W))
 // times `mul` as fp16 to dst[c_begin .. c_begin + W).
