@@ -12,6 +12,13 @@ events, rank 0 reports the max over ranks. FLOPs follow the reference (bench/ben
 ``--impl reference`` times the reference's CPU path (the oracle restatement of
 src/tattn/reference.py's tiled_forward/tiled_backward) on the host cores, on a bounded sample of the
 same workload, and prints the same JSON line with "impl": "reference".
+
+``--compare`` (one GPU) prints one JSON line per implementation and config, in the spirit of the
+reference's bench/bench.py comparison table (bench.py:62-76, 128-171): this library, torch's
+scaled_dot_product_attention with each backend (flash, cuDNN, memory-efficient) and a naive
+materialised softmax, each with fwd and fwd+bwd TFLOP/s, peak extra memory and the max-abs error of O
+and the gradients against an fp32 definition on two (b, h) pairs. The other implementations are
+library kernels shown for context only; they are not part of this library's path.
 """
 
 from __future__ import annotations
@@ -451,6 +458,96 @@ def run_gpu(args) -> None:
         dist.destroy_process_group()
 
 
+def run_compare(args) -> None:
+    """Comparison table (see the module docstring): one JSON line per (config, implementation)."""
+    import torch
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    from tattn import attention
+
+    dev = torch.device("cuda", 0)
+
+    def naive(q, k, v, causal, scale):
+        s_ = (q @ k.transpose(-1, -2)).float() * scale
+        if causal:
+            n_ = q.shape[-2]
+            s_ = s_.masked_fill(torch.ones(n_, n_, dtype=torch.bool, device=q.device).triu(1), float("-inf"))
+        return (torch.softmax(s_, -1).to(q.dtype) @ v)
+
+    def sdpa(backend):
+        def f(q, k, v, causal, scale):
+            with sdpa_kernel([backend]):
+                return F.scaled_dot_product_attention(q, k, v, is_causal=causal, scale=scale)
+        return f
+
+    impls = {
+        "tattn_b200": lambda q, k, v, causal, scale: attention(q, k, v, causal=causal, sm_scale=scale),
+        "sdpa_flash": sdpa(SDPBackend.FLASH_ATTENTION),
+        "sdpa_cudnn": sdpa(SDPBackend.CUDNN_ATTENTION),
+        "sdpa_efficient": sdpa(SDPBackend.EFFICIENT_ATTENTION),
+        "naive": naive,
+    }
+    for cfg in ("cfg2", "cfg3"):
+        b, h, n, d, causal = CONFIGS[cfg]
+        scale = 1.0 / math.sqrt(d)
+        g = torch.Generator(device=dev).manual_seed(1234)
+        q, k, v, do = (torch.randn((b, h, n, d), generator=g, device=dev).to(torch.float16) for _ in range(4))
+        # fp32 definition on two (b, h) pairs for the error columns
+        pairs = [(0, 0), (b - 1, h - 1)]
+        refs = {}
+        for bi, hi in pairs:
+            qf, kf, vf = (t[bi, hi].float().requires_grad_() for t in (q, k, v))
+            of = naive(qf, kf, vf, causal, scale)
+            gq, gk, gv = torch.autograd.grad(of, (qf, kf, vf), do[bi, hi].float())
+            refs[(bi, hi)] = (of.detach(), gq, gk, gv)
+        for name, fn in impls.items():
+            line = {"compare": name, "config": cfg, "shape": [b, h, n, d], "causal": causal}
+            try:
+                qg, kg, vg = (t.detach().requires_grad_() for t in (q, k, v))
+
+                def step():
+                    o_ = fn(qg, kg, vg, causal, scale)
+                    return o_, torch.autograd.grad(o_, (qg, kg, vg), do)
+
+                def fwd():
+                    with torch.no_grad():
+                        return fn(q, k, v, causal, scale)
+
+                o_, grads = step()
+                err = {"o": 0.0, "dq": 0.0, "dk": 0.0, "dv": 0.0}
+                for (bi, hi), (of, gq, gk, gv) in refs.items():
+                    for key, a_, r_ in (("o", o_, of), ("dq", grads[0], gq), ("dk", grads[1], gk), ("dv", grads[2], gv)):
+                        err[key] = max(err[key], (a_[bi, hi].float() - r_).abs().max().item())
+                del o_, grads
+                torch.cuda.synchronize()
+                base = torch.cuda.memory_allocated(dev)
+                torch.cuda.reset_peak_memory_stats(dev)
+                step()
+                torch.cuda.synchronize()
+                peak = torch.cuda.max_memory_allocated(dev) - base
+                for fn_, key in ((fwd, "fwd"), (step, "fwd+bwd")):
+                    for _ in range(3):
+                        fn_()
+                    torch.cuda.synchronize()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    iters = max(3, args.steps // 4)
+                    e0.record()
+                    for _ in range(iters):
+                        fn_()
+                    e1.record()
+                    torch.cuda.synchronize()
+                    ms = e0.elapsed_time(e1) / iters
+                    line[f"{key}_ms"] = round(ms, 4)
+                    line[f"{key}_tflops"] = round(flops(b, h, n, d, causal, key) / (ms * 1e-3) / 1e12, 1)
+                line["peak_extra_mib_fwd_bwd"] = round(peak / 2**20, 1)
+                line["max_abs_err_vs_fp32"] = {k_: float(f"{v_:.3g}") for k_, v_ in err.items()}
+            except Exception as e:  # a backend that does not support this GPU / shape
+                line["unavailable"] = f"{type(e).__name__}: {str(e).splitlines()[0][:160] if str(e) else ''}"
+            print(json.dumps(line), flush=True)
+            torch.cuda.empty_cache()
+
+
 def run_reference(args) -> None:
     """The reference's CPU implementation of the path (oracle port), rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
@@ -507,9 +604,14 @@ def main() -> None:
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU work for the CPU baseline")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--lean", action="store_true", help="warm-up + timed steps only (for profiler runs)")
+    ap.add_argument("--compare", action="store_true",
+                    help="comparison table against torch SDPA backends and a naive softmax (one GPU)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.compare:
+        run_compare(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
