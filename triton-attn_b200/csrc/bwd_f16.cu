@@ -18,10 +18,15 @@
 // their own, and the fp32 accumulators. Because nothing is overwritten in place, the S/dP MMAs of the
 // next block are issued as soon as the compute warps have loaded the current S and dP into registers,
 // and run on the tensor core while the compute warps turn them into P and dS.
-//   dQ, D <= 64:   128-key blocks, the warpgroups split each block's columns (64 each)
+//   dQ, D <= 64:   128-key blocks, the warpgroups split each block's columns (64 each); persistent
+//                  (one CTA per SM looping over query tiles) when not causal
 //   dQ, D = 128:   64-key blocks, the warpgroups take alternate blocks and ping-pong (the 128-key
 //                  layout leaves room for only two K/V ring stages at this head dim)
-//   dK/dV:         128-query blocks (64 at D = 128), the warpgroups split each block's columns
+//   dK/dV:         128-query blocks (64 at D = 128), the warpgroups split each block's columns;
+//                  persistent when not causal and D <= 64
+// Persistent kernels write their outputs through shared-memory staging and TMA stores; causal grids
+// keep one tile per CTA, because their tiles differ in cost and the hardware's dynamic CTA scheduling
+// balances them (static round-robin was measured 6-12% slower there).
 // 128-wide blocks keep every S/dP MMA at N = 128, where the tensor core, not shared-memory bandwidth,
 // sets the rate (an N = 64 MMA with both operands in shared memory is bandwidth-bound at 2/3 rate).
 //
@@ -369,6 +374,322 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------- dQ, D <= 64: persistent
+// One CTA per SM looping over 128-row query tiles (static round-robin over the same order as the
+// one-tile-per-CTA grid: longest-first when causal). Q/dO tiles are double-buffered, the K/V ring and
+// every barrier phase run on across tiles (g = global key-block index, it = tile iteration), the next
+// tile's first S/dP MMAs go out while the current tile finishes, each compute warp writes its 32 rows
+// of its warpgroup's dQ columns through shared-memory staging and a TMA store, and M/delta of the next
+// tile are fetched before the current tile's epilogue. The first dQ MMA of a tile waits until the
+// compute warps have read the previous tile's accumulator (dq_read).
+template <int D>
+struct DqPersistCfg {
+  using G = Geo<D>;
+  static_assert(D <= 64, "persistent dQ: 128-key blocks");
+  static constexpr int BK = 128, H = 64;
+  static constexpr int NS = 3;                          // K/V ring stages
+  static constexpr int T_ROW = G::tile(128);            // [128, D] tile
+  static constexpr int HW = D / 2;                      // dQ columns per compute warpgroup
+  static constexpr int SWB_O = HW * 2;                  // staging row bytes (swizzle span of the store map)
+  static constexpr int STG = 32 * SWB_O;                // per-warp staging: 32 rows x D/2 fp16
+  static constexpr int OFF_Q = 0;                       // [2 buffers]
+  static constexpr int OFF_DO = 2 * T_ROW;              // [2 buffers]
+  static constexpr int OFF_K = 4 * T_ROW;               // NS key blocks
+  static constexpr int OFF_V = OFF_K + NS * T_ROW;      // NS value blocks
+  static constexpr int OFF_STG = OFF_V + NS * T_ROW;    // 8 compute warps x STG
+  static constexpr int OFF_BAR = OFF_STG + 8 * (STG < 1024 ? 1024 : STG);
+  // q_full[2], q_empty[2], kv_full[NS], kv_empty[NS], s_full, s_free, ds_full, ds_free, dq_done,
+  // dq_read, fin[3]
+  static constexpr int NBARS = 4 + 2 * NS + 9;
+  static constexpr int OFF_MISC = OFF_BAR + NBARS * 8;
+  static constexpr int SMEM_USED = OFF_MISC + 16;
+  static constexpr int SMEM_BYTES = (SMEM_USED > 118784 ? SMEM_USED : 118784) + 1024;
+  static constexpr uint32_t T_S = 0, T_DP = 128, T_DS = 256, T_DQ = 320;
+  static_assert(T_DQ + D <= 512, "TMEM budget");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+  static_assert(OFF_STG % 1024 == 0, "staging alignment");
+  static constexpr uint32_t IDESC_S = idesc_f16_f32(128, BK, false);
+  static constexpr uint32_t IDESC_DQ = idesc_f16_f32(128, D, true);
+};
+
+// Query tile `tile` of the one-tile-per-CTA order: (b*h index, query tile), longest first when causal.
+__device__ __forceinline__ void dq_tile(int tile, int nct, int zh, bool causal, int* bh, int* qt) {
+  if (causal) {
+    *bh = tile % zh;
+    *qt = nct - 1 - tile / zh;
+  } else {
+    *bh = tile / nct;
+    *qt = tile % nct;
+  }
+}
+
+template <int D, bool CAUSAL>
+__global__ void __launch_bounds__(kThreads, 1)
+    bwd_dq_persist_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                          const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                          const __grid_constant__ CUtensorMap tm_dq, const BwdArgs args) {
+  using C = DqPersistCfg<D>;
+  using G = Geo<D>;
+  constexpr int H = C::H, NS = C::NS, HW = C::HW;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base_u32 - raw_u32);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* bar_q_full = bars;                  // [2] Q/dO buffer landed
+  uint64_t* bar_q_empty = bars + 2;             // [2] every S/dP MMA of the buffer's tile has completed
+  uint64_t* bar_kv_full = bars + 4;             // [NS]
+  uint64_t* bar_kv_empty = bars + 4 + NS;       // [NS]
+  uint64_t* bar_s_full = bars + 4 + 2 * NS;
+  uint64_t* bar_s_free = bar_s_full + 1;
+  uint64_t* bar_ds_full = bar_s_full + 2;
+  uint64_t* bar_ds_free = bar_s_full + 3;
+  uint64_t* bar_dq_done = bar_s_full + 4;
+  uint64_t* bar_dq_read = bar_s_full + 5;       // the compute warps hold the tile's dQ in registers
+  uint64_t* bar_fin = bar_s_full + 6;           // [3]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+  const CtaAbort ab{abort_flag, args.status};
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int N = args.N;
+  const int zh = args.Z * args.H;
+  const int nct = (N + 127) / 128;
+  const int ntiles = nct * zh;
+  const int NBk = (N + C::BK - 1) / C::BK;
+  auto tile_n = [&](int qt) { return CAUSAL ? min(qt + 1, NBk) : NBk; };  // key blocks of query tile qt
+
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bar_q_full[b], 1);
+      mbar_init(&bar_q_empty[b], 1);
+    }
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&bar_kv_full[s], 1);
+      mbar_init(&bar_kv_empty[s], 2);  // S/dP issuer + dQ issuer
+    }
+    mbar_init(bar_s_full, 1);
+    mbar_init(bar_s_free, 256);
+    mbar_init(bar_ds_full, 256);
+    mbar_init(bar_ds_free, 1);
+    mbar_init(bar_dq_done, 1);
+    mbar_init(bar_dq_read, 256);
+    for (int i = 0; i < 3; ++i) mbar_init(&bar_fin[i], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kAllocWarp) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  if (warp == kTmaWarp && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+    tma_prefetch_desc(&tm_do);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sQ = base_u32 + C::OFF_Q, sDO = base_u32 + C::OFF_DO;
+  const uint32_t sK = base_u32 + C::OFF_K, sV = base_u32 + C::OFF_V;
+
+  if (warp >= kTmaWarp) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
+    if (warp == kTmaWarp && lane == 0) {
+      // -------------------------------------------------------------- TMA producer
+      int g = 0, it = 0, q_issued = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
+        int bh, qt;
+        dq_tile(tile, nct, zh, CAUSAL, &bh, &qt);
+        const int zi = bh / args.H, hi = bh % args.H, n = tile_n(qt);
+        const int qb = it & 1;
+        if (it >= 2 && !mbar_wait(&bar_q_empty[qb], ((it >> 1) - 1) & 1, ab)) { ok = false; break; }
+        mbar_arrive_expect_tx(&bar_q_full[qb], 2 * C::T_ROW);
+        for (int ch = 0; ch < G::NCH; ++ch) {
+          tma_load_4d(sQ + qb * C::T_ROW + ch * G::chunk(128), &tm_q, ch * G::CW, 128 * qt, hi, zi, &bar_q_full[qb]);
+          tma_load_4d(sDO + qb * C::T_ROW + ch * G::chunk(128), &tm_do, ch * G::CW, 128 * qt, hi, zi, &bar_q_full[qb]);
+        }
+        ++q_issued;
+        for (int c = 0; c < n; ++c, ++g) {
+          const int st = g % NS;
+          if (g >= NS && !mbar_wait(&bar_kv_empty[st], ((g / NS) - 1) & 1, ab)) { ok = false; break; }
+          mbar_arrive_expect_tx(&bar_kv_full[st], 2 * C::T_ROW);
+          for (int ch = 0; ch < G::NCH; ++ch) {
+            tma_load_4d(sK + st * C::T_ROW + ch * G::chunk(128), &tm_k, ch * G::CW, c * C::BK, hi, zi, &bar_kv_full[st]);
+            tma_load_4d(sV + st * C::T_ROW + ch * G::chunk(128), &tm_v, ch * G::CW, c * C::BK, hi, zi, &bar_kv_full[st]);
+          }
+        }
+      }
+      for (int ii = max(0, q_issued - 2); ii < q_issued; ++ii) mbar_drain(&bar_q_full[ii & 1], (ii >> 1) & 1, kDrainNs);
+      for (int gg = max(0, g - NS); gg < g; ++gg) mbar_drain(&bar_kv_full[gg % NS], (gg / NS) & 1, kDrainNs);
+    } else if (warp == kMmaSWarp) {
+      // -------------------------------------------------------------- S/dP issuer
+      const uint32_t idesc_s = C::IDESC_S | (args.negate_s ? (1u << 13) : 0u);
+      const uint64_t dQ = smem_desc(sQ, 16, 8 * G::SWB, G::LAYOUT);
+      const uint64_t dDO = smem_desc(sDO, 16, 8 * G::SWB, G::LAYOUT);
+      const uint64_t dK = smem_desc(sK, 16, 8 * G::SWB, G::LAYOUT);
+      const uint64_t dV = smem_desc(sV, 16, 8 * G::SWB, G::LAYOUT);
+      int g = 0, it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
+        int bh, qt;
+        dq_tile(tile, nct, zh, CAUSAL, &bh, &qt);
+        const int n = tile_n(qt);
+        const int qb = it & 1;
+        if (!warp_wait(&bar_q_full[qb], (it >> 1) & 1, ab)) { ok = false; break; }
+        const uint64_t qo = uint64_t((qb * C::T_ROW) >> 4);
+        for (int c = 0; c < n; ++c, ++g) {
+          if (g > 0 && !warp_wait(bar_s_free, (g - 1) & 1, ab)) { ok = false; break; }
+          if (!warp_wait(&bar_kv_full[g % NS], (g / NS) & 1, ab)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t so = uint64_t(((g % NS) * C::T_ROW) >> 4);
+          mma_kmajor<D, G::chunk(128), G::chunk(128)>(tmem + C::T_S, dQ + qo, dK + so, idesc_s);
+          mma_kmajor<D, G::chunk(128), G::chunk(128)>(tmem + C::T_DP, dDO + qo, dV + so, C::IDESC_S);
+          mma_commit_elect(bar_s_full);
+          mma_commit_elect(&bar_kv_empty[g % NS]);
+        }
+        mma_commit_elect(&bar_q_empty[qb]);  // the buffer's Q/dO have been read by every MMA of this tile
+      }
+      mma_commit_elect(&bar_fin[0]);
+      mbar_drain(&bar_fin[0], 0, kDrainNs);
+    } else if (warp == kMmaAccWarp) {
+      // -------------------------------------------------------------- dQ issuer
+      const uint64_t dKmn = smem_desc(sK, G::chunk(128), 8 * G::SWB, G::LAYOUT);
+      int g = 0, it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
+        int bh, qt;
+        dq_tile(tile, nct, zh, CAUSAL, &bh, &qt);
+        const int n = tile_n(qt);
+        // This tile's first MMA overwrites the accumulator: the previous epilogue must have read it.
+        if (it > 0 && !warp_wait(bar_dq_read, (it - 1) & 1, ab)) { ok = false; break; }
+        for (int c = 0; c < n; ++c, ++g) {
+          // kv_full is complete already (the S MMA of block g needed it); waiting on it orders the K reads.
+          if (!warp_wait(bar_ds_full, g & 1, ab) || !warp_wait(&bar_kv_full[g % NS], (g / NS) & 1, ab)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          mma_tmem_mn<D, C::BK / 16>(tmem + C::T_DQ, tmem + C::T_DS, dKmn + uint64_t(((g % NS) * C::T_ROW) >> 4),
+                                     C::IDESC_DQ, c > 0 ? 1u : 0u);
+          mma_commit_elect(bar_ds_free);
+          mma_commit_elect(&bar_kv_empty[g % NS]);
+        }
+        if (ok) mma_commit_elect(bar_dq_done);
+      }
+      mma_commit_elect(&bar_fin[2]);
+      mbar_drain(&bar_fin[2], 0, kDrainNs);
+    }
+  } else {
+    // ------------------------------------------------------------------ compute warpgroups
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kComputeRegs));
+    const int w = warp / 4;            // column half of every key block, and of dQ
+    const int r = threadIdx.x % 128;   // query row within the tile = TMEM lane
+    const int q4 = warp % 4;
+    const uint32_t tl = tmem + (uint32_t(q4 * 32) << 16);
+    const uint32_t stg = base_u32 + C::OFF_STG + warp * (C::STG < 1024 ? 1024 : C::STG);
+    const uint64_t scale2 = f2(args.qk_scale, args.qk_scale);
+    int g = 0, it = 0;
+    bool ok = true;
+    // M and delta of this thread's row in the first tile; later tiles' are fetched one tile ahead.
+    float m_nx = 0.f, d_nx = 0.f;
+    if (blockIdx.x < ntiles) {
+      int bh, qt;
+      dq_tile(blockIdx.x, nct, zh, CAUSAL, &bh, &qt);
+      const int row = 128 * qt + r;
+      if (row < N) {
+        m_nx = args.m[int64_t(bh) * N + row];
+        d_nx = args.delta[int64_t(bh) * N + row];
+      }
+    }
+    for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
+      int bh, qt;
+      dq_tile(tile, nct, zh, CAUSAL, &bh, &qt);
+      const int zi = bh / args.H, hi = bh % args.H, q0 = 128 * qt, n = tile_n(qt);
+      const int row = q0 + r;
+      const uint64_t negm2 = f2(-m_nx, -m_nx), negd2 = f2(-d_nx, -d_nx);
+      const int row_lim = CAUSAL ? min(N, row + 1) : N;  // valid key columns: key < row_lim
+      for (int c = 0; c < n; ++c, ++g) {
+        if (!warp_wait(bar_s_full, g & 1, ab)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t s[H], dp[H];
+        tmem_load_cols<H>(tl + C::T_S + w * H, s);
+        tmem_load_cols<H>(tl + C::T_DP + w * H, dp);
+        tmem_wait_ld();
+        reg_fence<H>(s);
+        reg_fence<H>(dp);
+        tc_fence_before();
+        mbar_arrive(bar_s_free);  // the tensor core may now write S/dP of the next block
+        const int k0 = c * C::BK + w * H;
+        const bool masked = (k0 + H > N) || (CAUSAL && k0 + H - 1 > q0);
+        uint32_t ds[H / 2];
+        if (masked)
+          ds_row64<true>(s, dp, ds, scale2, negm2, negd2, row_lim - k0);
+        else
+          ds_row64<false>(s, dp, ds, scale2, negm2, negd2, 0);
+        if (g > 0) {  // the dQ MMA of the previous block has read dS
+          if (!warp_wait(bar_ds_free, (g - 1) & 1, ab)) { ok = false; break; }
+          tc_fence_after();
+        }
+        tmem_store_cols<H / 2>(tl + C::T_DS + w * (H / 2), ds);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar_ds_full);
+      }
+      if (!ok) break;
+      // M and delta of the next tile's row, in flight during this epilogue.
+      if (tile + int(gridDim.x) < ntiles) {
+        int bh2, qt2;
+        dq_tile(tile + gridDim.x, nct, zh, CAUSAL, &bh2, &qt2);
+        const int row2 = 128 * qt2 + r;
+        m_nx = row2 < N ? args.m[int64_t(bh2) * N + row2] : 0.f;
+        d_nx = row2 < N ? args.delta[int64_t(bh2) * N + row2] : 0.f;
+      }
+      if (!warp_wait(bar_dq_done, it & 1, ab)) { ok = false; break; }
+      // ---- epilogue: this warpgroup's dQ columns [w*HW, w*HW + HW) * sm_scale, 32 rows per warp
+      tc_fence_after();
+      uint32_t o[HW];
+      tmem_load_cols<HW>(tl + C::T_DQ + w * HW, o);
+      tmem_wait_ld();
+      reg_fence<HW>(o);
+      tc_fence_before();
+      mbar_arrive(bar_dq_read);  // the next tile's first dQ MMA may overwrite the accumulator
+      if (lane == 0) tma_store_wait_read_all();  // this warp's previous store has left the staging area
+      __syncwarp();
+      const float mul = args.sm_scale;
+#pragma unroll
+      for (int u = 0; u < C::SWB_O / 16; ++u) {
+        const int c = u * 8;
+        const uint32_t addr = stg + swizzle_offset<C::SWB_O>(uint32_t(lane * C::SWB_O + u * 16));
+        const uint32_t h0 = pack_half2(__uint_as_float(o[c + 0]) * mul, __uint_as_float(o[c + 1]) * mul);
+        const uint32_t h1 = pack_half2(__uint_as_float(o[c + 2]) * mul, __uint_as_float(o[c + 3]) * mul);
+        const uint32_t h2 = pack_half2(__uint_as_float(o[c + 4]) * mul, __uint_as_float(o[c + 5]) * mul);
+        const uint32_t h3 = pack_half2(__uint_as_float(o[c + 6]) * mul, __uint_as_float(o[c + 7]) * mul);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(h0), "r"(h1), "r"(h2), "r"(h3)
+                     : "memory");
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {  // rows past N are clipped by the tensor map
+        tma_store_4d(&tm_dq, stg, w * HW, q0 + 32 * q4, hi, zi);
+        tma_store_commit();
+      }
+    }
+    if (lane == 0) tma_store_wait_all();  // the staging area must stay valid until the stores are done
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kAllocWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // ------------------------------------------------------- dQ, D = 128: alternating 64-key blocks
 // One CTA per 128-row query tile; key blocks of 64 rows. (128-key blocks as above would leave room for
 // only two K/V ring stages at D = 128.) Compute warpgroup w takes the blocks c with c % 2 == w, each
@@ -684,6 +1005,342 @@ __device__ __forceinline__ void dkdv_producer(const CUtensorMap* tm_q, const CUt
   }
 }
 
+// ------------------------------------------------------------------- dK/dV, D <= 64: persistent
+// One CTA per SM looping over 128-row key tiles (static round-robin over the same longest-first tile
+// order as the one-tile-per-CTA grid), so a tile's setup, first loads and epilogue overlap its
+// neighbours' work: K/V tiles are double-buffered (the next tile's are loaded during the current one),
+// the Q/dO ring and every barrier phase run on across tiles (counters g = global block index and
+// it = tile iteration), the next tile's first S^T/dP^T MMAs are issued as soon as the current tile's
+// last ones are in registers, and dV/dK leave through per-warp shared-memory staging and TMA stores
+// instead of per-thread row stores. The first dV/dK MMA of a tile waits until the compute warps have
+// read the previous tile's accumulators (acc_read).
+template <int D>
+struct DkvPersistCfg {
+  using G = Geo<D>;
+  static_assert(D <= 64, "persistent dK/dV: 128-query blocks");
+  static constexpr int BQ = 128, H = 64;
+  static constexpr int NS = 4;                            // Q/dO ring stages
+  static constexpr int T_KEY = G::tile(128);
+  static constexpr int T_Q = G::tile(BQ);
+  static constexpr int HW = D / 2;                        // columns per store round (two rounds)
+  static constexpr int SWB_O = HW * 2;                    // staging row bytes (swizzle span of the store map)
+  static constexpr int STG = 32 * SWB_O < 1024 ? 1024 : 32 * SWB_O;  // per-warp staging: 32 rows x D/2 fp16
+  static constexpr int OFF_K = 0;                         // [2 buffers] key tiles
+  static constexpr int OFF_V = 2 * T_KEY;                 // [2 buffers] value tiles
+  static constexpr int OFF_Q = 4 * T_KEY;                 // NS query blocks
+  static constexpr int OFF_DO = OFF_Q + NS * T_Q;         // NS dO blocks
+  static constexpr int OFF_STG = OFF_DO + NS * T_Q;       // 8 compute warps x STG (1024-aligned)
+  static constexpr int OFF_MD = OFF_STG + 8 * STG;        // NS x (BQ -M | BQ -delta) fp32
+  static constexpr int OFF_BAR = OFF_MD + NS * 2 * BQ * 4;
+  // kv_full[2], kv_empty[2], q_full[NS], md_full[NS], q_empty[NS], s_full, s_free, p_full, acc_free,
+  // acc_done, acc_read, fin[3]
+  static constexpr int NBARS = 4 + 3 * NS + 9;
+  static constexpr int OFF_MISC = OFF_BAR + NBARS * 8;
+  static constexpr int SMEM_USED = OFF_MISC + 16;
+  static constexpr int SMEM_BYTES = (SMEM_USED > 118784 ? SMEM_USED : 118784) + 1024;
+  static constexpr uint32_t T_ST = 0, T_DPT = BQ, T_PT = 2 * BQ, T_DST = 2 * BQ + BQ / 2;
+  static constexpr uint32_t T_DV = 3 * BQ, T_DK = 3 * BQ + D;
+  static_assert(3 * BQ + 2 * D <= 512, "TMEM budget");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+  static_assert(OFF_STG % 1024 == 0 && STG % 1024 == 0, "staging alignment");
+  static constexpr uint32_t IDESC_S = idesc_f16_f32(128, BQ, false);
+  static constexpr uint32_t IDESC_ACC = idesc_f16_f32(128, D, true);
+};
+
+// Tile `tile` of the longest-first order (as cta_order over the same grid): (b*h index, key tile).
+__device__ __forceinline__ void dkdv_tile(int tile, int nct, int zh, bool causal, int* bh, int* kt) {
+  if (causal) {
+    *bh = tile % zh;
+    *kt = tile / zh;
+  } else {
+    *bh = tile / nct;
+    *kt = tile % nct;
+  }
+}
+
+template <int D, bool CAUSAL>
+__global__ void __launch_bounds__(kThreads, 1)
+    bwd_dkdv_persist_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                            const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                            const __grid_constant__ CUtensorMap tm_dk, const __grid_constant__ CUtensorMap tm_dv,
+                            const BwdArgs args) {
+  using C = DkvPersistCfg<D>;
+  using G = Geo<D>;
+  constexpr int H = C::H, BQ = C::BQ, NS = C::NS;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base_u32 - raw_u32);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* bar_kv_full = bars;                 // [2] key/value buffer landed
+  uint64_t* bar_kv_empty = bars + 2;            // [2] every S^T/dP^T MMA of the buffer's tile has completed
+  uint64_t* bar_q_full = bars + 4;              // [NS]
+  uint64_t* bar_md_full = bars + 4 + NS;        // [NS]
+  uint64_t* bar_q_empty = bars + 4 + 2 * NS;    // [NS]
+  uint64_t* bar_s_full = bars + 4 + 3 * NS;
+  uint64_t* bar_s_free = bar_s_full + 1;
+  uint64_t* bar_p_full = bar_s_full + 2;
+  uint64_t* bar_acc_free = bar_s_full + 3;
+  uint64_t* bar_acc_done = bar_s_full + 4;
+  uint64_t* bar_acc_read = bar_s_full + 5;      // the compute warps hold the tile's dV/dK in registers
+  uint64_t* bar_fin = bar_s_full + 6;           // [3]
+  float* md = reinterpret_cast<float*>(smem + C::OFF_MD);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+  const CtaAbort ab{abort_flag, args.status};
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int N = args.N;
+  const int zh = args.Z * args.H;
+  const int nct = (N + 127) / 128;
+  const int ntiles = nct * zh;
+  const int NBq = (N + BQ - 1) / BQ;
+  // Query blocks of a key tile kt: [lo, NBq).
+  auto tile_lo = [&](int kt) { return CAUSAL ? (128 * kt) / BQ : 0; };
+
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bar_kv_full[b], 1);
+      mbar_init(&bar_kv_empty[b], 1);
+    }
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&bar_q_full[s], 1);
+      mbar_init(&bar_md_full[s], 32);
+      mbar_init(&bar_q_empty[s], 2);  // S^T/dP^T issuer + dV/dK issuer
+    }
+    mbar_init(bar_s_full, 1);
+    mbar_init(bar_s_free, 256);
+    mbar_init(bar_p_full, 256);
+    mbar_init(bar_acc_free, 1);
+    mbar_init(bar_acc_done, 1);
+    mbar_init(bar_acc_read, 256);
+    for (int i = 0; i < 3; ++i) mbar_init(&bar_fin[i], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kAllocWarp) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  if (warp == kTmaWarp && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+    tma_prefetch_desc(&tm_do);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sK = base_u32 + C::OFF_K, sV = base_u32 + C::OFF_V;
+  const uint32_t sQ = base_u32 + C::OFF_Q, sDO = base_u32 + C::OFF_DO;
+
+  if (warp >= kTmaWarp) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
+    if (warp == kTmaWarp) {
+      // -------------------------------------------------------------- TMA producer + -M/-delta staging
+      int g = 0, it = 0, kv_issued = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
+        int bh, kt;
+        dkdv_tile(tile, nct, zh, CAUSAL, &bh, &kt);
+        const int zi = bh / args.H, hi = bh % args.H, k0 = 128 * kt, lo = tile_lo(kt), n = NBq - lo;
+        const int kb = it & 1;
+        if (it >= 2 && !warp_wait(&bar_kv_empty[kb], ((it >> 1) - 1) & 1, ab)) { ok = false; break; }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&bar_kv_full[kb], 2 * C::T_KEY);
+          for (int ch = 0; ch < G::NCH; ++ch) {
+            tma_load_4d(sK + kb * C::T_KEY + ch * G::chunk(128), &tm_k, ch * G::CW, k0, hi, zi, &bar_kv_full[kb]);
+            tma_load_4d(sV + kb * C::T_KEY + ch * G::chunk(128), &tm_v, ch * G::CW, k0, hi, zi, &bar_kv_full[kb]);
+          }
+        }
+        ++kv_issued;
+        const float* mrow = args.m + int64_t(bh) * N;
+        const float* drow = args.delta + int64_t(bh) * N;
+        for (int c = 0; c < n; ++c, ++g) {
+          const int st = g % NS;
+          if (g >= NS && !warp_wait(&bar_q_empty[st], ((g / NS) - 1) & 1, ab)) { ok = false; break; }
+          const int qr = (lo + c) * BQ;
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&bar_q_full[st], 2 * C::T_Q);
+            for (int ch = 0; ch < G::NCH; ++ch) {
+              tma_load_4d(sQ + st * C::T_Q + ch * G::chunk(BQ), &tm_q, ch * G::CW, qr, hi, zi, &bar_q_full[st]);
+              tma_load_4d(sDO + st * C::T_Q + ch * G::chunk(BQ), &tm_do, ch * G::CW, qr, hi, zi, &bar_q_full[st]);
+            }
+          }
+          float* slot = md + st * 2 * BQ;
+#pragma unroll
+          for (int j = lane; j < BQ; j += 32) {
+            const int q = qr + j;
+            slot[j] = q < N ? -mrow[q] : 0.f;
+            slot[BQ + j] = q < N ? -drow[q] : 0.f;
+          }
+          mbar_arrive(&bar_md_full[st]);
+        }
+      }
+      // Every copy issued must land before the CTA exits (instant on the normal path).
+      if (lane == 0) {
+        for (int ii = max(0, kv_issued - 2); ii < kv_issued; ++ii) mbar_drain(&bar_kv_full[ii & 1], (ii >> 1) & 1, kDrainNs);
+        for (int gg = max(0, g - NS); gg < g; ++gg) mbar_drain(&bar_q_full[gg % NS], (gg / NS) & 1, kDrainNs);
+      }
+    } else if (warp == kMmaSWarp) {
+      // -------------------------------------------------------------- S^T/dP^T issuer
+      const uint32_t idesc_s = C::IDESC_S | (args.negate_s ? (1u << 13) : 0u);
+      const uint64_t dK = smem_desc(sK, 16, 8 * G::SWB, G::LAYOUT);
+      const uint64_t dV = smem_desc(sV, 16, 8 * G::SWB, G::LAYOUT);
+      const uint64_t dQ = smem_desc(sQ, 16, 8 * G::SWB, G::LAYOUT);
+      const uint64_t dDO = smem_desc(sDO, 16, 8 * G::SWB, G::LAYOUT);
+      int g = 0, it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
+        int bh, kt;
+        dkdv_tile(tile, nct, zh, CAUSAL, &bh, &kt);
+        const int n = NBq - tile_lo(kt);
+        const int kb = it & 1;
+        if (!warp_wait(&bar_kv_full[kb], (it >> 1) & 1, ab)) { ok = false; break; }
+        const uint64_t ko = uint64_t((kb * C::T_KEY) >> 4);
+        for (int c = 0; c < n; ++c, ++g) {
+          if (g > 0 && !warp_wait(bar_s_free, (g - 1) & 1, ab)) { ok = false; break; }
+          if (!warp_wait(&bar_q_full[g % NS], (g / NS) & 1, ab)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t so = uint64_t(((g % NS) * C::T_Q) >> 4);
+          mma_kmajor<D, G::chunk(128), G::chunk(BQ)>(tmem + C::T_ST, dK + ko, dQ + so, idesc_s);
+          mma_kmajor<D, G::chunk(128), G::chunk(BQ)>(tmem + C::T_DPT, dV + ko, dDO + so, C::IDESC_S);
+          mma_commit_elect(bar_s_full);
+          mma_commit_elect(&bar_q_empty[g % NS]);
+        }
+        mma_commit_elect(&bar_kv_empty[kb]);  // the buffer's K/V have been read by every MMA of this tile
+      }
+      mma_commit_elect(&bar_fin[0]);
+      mbar_drain(&bar_fin[0], 0, kDrainNs);
+    } else if (warp == kMmaAccWarp) {
+      // -------------------------------------------------------------- dV/dK issuer
+      const uint64_t dQmn = smem_desc(sQ, G::chunk(BQ), 8 * G::SWB, G::LAYOUT);
+      const uint64_t dDOmn = smem_desc(sDO, G::chunk(BQ), 8 * G::SWB, G::LAYOUT);
+      int g = 0, it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
+        int bh, kt;
+        dkdv_tile(tile, nct, zh, CAUSAL, &bh, &kt);
+        const int n = NBq - tile_lo(kt);
+        // The accumulators are overwritten by this tile's first MMAs: the previous tile's epilogue
+        // must have read them.
+        if (it > 0 && !warp_wait(bar_acc_read, (it - 1) & 1, ab)) { ok = false; break; }
+        for (int c = 0; c < n; ++c, ++g) {
+          // q_full is complete already (the S^T MMA of block g needed it); waiting on it orders the reads.
+          if (!warp_wait(bar_p_full, g & 1, ab) || !warp_wait(&bar_q_full[g % NS], (g / NS) & 1, ab)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t so = uint64_t(((g % NS) * C::T_Q) >> 4);
+          mma_tmem_mn<D, BQ / 16>(tmem + C::T_DV, tmem + C::T_PT, dDOmn + so, C::IDESC_ACC, c > 0 ? 1u : 0u);
+          mma_tmem_mn<D, BQ / 16>(tmem + C::T_DK, tmem + C::T_DST, dQmn + so, C::IDESC_ACC, c > 0 ? 1u : 0u);
+          mma_commit_elect(bar_acc_free);
+          mma_commit_elect(&bar_q_empty[g % NS]);
+        }
+        if (ok) mma_commit_elect(bar_acc_done);
+      }
+      mma_commit_elect(&bar_fin[2]);
+      mbar_drain(&bar_fin[2], 0, kDrainNs);
+    } else {
+      // warp 11: allocated TMEM above; nothing else until the teardown
+    }
+  } else {
+    // ------------------------------------------------------------------ compute warpgroups
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kComputeRegs));
+    const int w = warp / 4;            // column half of every query block; 0 writes dV, 1 writes dK
+    const int r = threadIdx.x % 128;   // key row within the tile = TMEM lane
+    const int q4 = warp % 4;           // TMEM lane quadrant: rows [32 q4, 32 q4 + 32)
+    const uint32_t tl = tmem + (uint32_t(q4 * 32) << 16);
+    const uint32_t stg = base_u32 + C::OFF_STG + warp * C::STG;
+    const uint64_t scale2 = f2(args.qk_scale, args.qk_scale);
+    const CUtensorMap* tm_out = w ? &tm_dk : &tm_dv;
+    const float mul = w ? args.sm_scale : 1.f;
+    int g = 0, it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
+      int bh, kt;
+      dkdv_tile(tile, nct, zh, CAUSAL, &bh, &kt);
+      const int zi = bh / args.H, hi = bh % args.H, k0 = 128 * kt, lo = tile_lo(kt), n = NBq - lo;
+      const int key = k0 + r;
+      for (int c = 0; c < n; ++c, ++g) {
+        const int st = g % NS;
+        if (!warp_wait(bar_s_full, g & 1, ab)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t s[H], dp[H];
+        tmem_load_cols<H>(tl + C::T_ST + w * H, s);
+        tmem_load_cols<H>(tl + C::T_DPT + w * H, dp);
+        tmem_wait_ld();
+        reg_fence<H>(s);
+        reg_fence<H>(dp);
+        tc_fence_before();
+        mbar_arrive(bar_s_free);  // the tensor core may now write S^T/dP^T of the next block
+        if (!warp_wait(&bar_md_full[st], (g / NS) & 1, ab)) { ok = false; break; }
+        const float* mq = md + st * 2 * BQ + w * H;
+        const int q0 = (lo + c) * BQ + w * H;  // first query column of this warpgroup's half
+        const bool masked = (q0 + H > N) || (k0 + 128 > N) || (CAUSAL && q0 < k0 + 127);
+        const int c_lo = CAUSAL ? max(0, key - q0) : 0;  // valid query columns: c_lo <= c < c_hi
+        const int c_hi = key < N ? N - q0 : 0;
+        uint32_t pt[H / 2], dst[H / 2];
+        if (masked)
+          pds_row<H, true>(s, dp, mq, mq + BQ, pt, dst, scale2, c_lo, c_hi);
+        else
+          pds_row<H, false>(s, dp, mq, mq + BQ, pt, dst, scale2, c_lo, c_hi);
+        if (g > 0) {  // the dV/dK MMAs of the previous block have read P^T/dS^T
+          if (!warp_wait(bar_acc_free, (g - 1) & 1, ab)) { ok = false; break; }
+          tc_fence_after();
+        }
+        tmem_store_cols<H / 2>(tl + C::T_PT + w * (H / 2), pt);
+        tmem_store_cols<H / 2>(tl + C::T_DST + w * (H / 2), dst);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar_p_full);
+      }
+      if (!ok || !warp_wait(bar_acc_done, it & 1, ab)) { ok = false; break; }
+      // ---- epilogue: dV (warpgroup 0) or dK * sm_scale (warpgroup 1), 32 rows per warp via TMA stores
+      tc_fence_after();
+      uint32_t o[D];
+      tmem_load_cols<D>(tl + (w ? C::T_DK : C::T_DV), o);
+      tmem_wait_ld();
+      reg_fence<D>(o);
+      tc_fence_before();
+      mbar_arrive(bar_acc_read);  // the next tile's first dV/dK MMAs may overwrite the accumulators
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {  // columns [half * HW, half * HW + HW)
+        if (lane == 0) tma_store_wait_read_all();  // this warp's previous store has left the staging area
+        __syncwarp();
+#pragma unroll
+        for (int u = 0; u < C::SWB_O / 16; ++u) {
+          const int c = half * C::HW + u * 8;
+          const uint32_t addr = stg + swizzle_offset<C::SWB_O>(uint32_t(lane * C::SWB_O + u * 16));
+          const uint32_t h0 = pack_half2(__uint_as_float(o[c + 0]) * mul, __uint_as_float(o[c + 1]) * mul);
+          const uint32_t h1 = pack_half2(__uint_as_float(o[c + 2]) * mul, __uint_as_float(o[c + 3]) * mul);
+          const uint32_t h2 = pack_half2(__uint_as_float(o[c + 4]) * mul, __uint_as_float(o[c + 5]) * mul);
+          const uint32_t h3 = pack_half2(__uint_as_float(o[c + 6]) * mul, __uint_as_float(o[c + 7]) * mul);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(h0), "r"(h1), "r"(h2), "r"(h3)
+                       : "memory");
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {  // rows past N are clipped by the tensor map
+          tma_store_4d(tm_out, stg, half * C::HW, k0 + 32 * q4, hi, zi);
+          tma_store_commit();
+        }
+      }
+    }
+    if (lane == 0) tma_store_wait_all();  // the staging area must stay valid until the stores are done
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kAllocWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // ------------------------------------------------------------------------- dK/dV: split columns
 // One CTA per 128-row key tile; query blocks of BQ (128, or 64 at D = 128 for the TMEM budget) whose
 // columns the two compute warpgroups split (warpgroup w takes columns [w*H, w*H + H), H = BQ/2).
@@ -910,59 +1567,106 @@ cudaError_t launch_common(Kern kern, int smem, long long grid, const CUtensorMap
   return cudaGetLastError();
 }
 
+int sm_count();
+
 template <int D, bool CAUSAL>
 cudaError_t dq_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tdo,
-                    const BwdArgs& a, cudaStream_t s) {
-  const long long grid = (long long)((a.N + 127) / 128) * a.Z * a.H;
-  if constexpr (D <= 64)
-    return launch_common(bwd_dq_split_kernel<D, CAUSAL>, DqSplitCfg<D>::SMEM_BYTES, grid, tq, tk, tv, tdo, a, s);
-  else
-    return launch_common(bwd_dq_alt_kernel<D, CAUSAL>, DqAltCfg<D>::SMEM_BYTES, grid, tq, tk, tv, tdo, a, s);
+                    const CUtensorMap& tdq, const BwdArgs& a, cudaStream_t s) {
+  const long long tiles = (long long)((a.N + 127) / 128) * a.Z * a.H;
+  if constexpr (D <= 64 && !CAUSAL) {  // persistent only when every tile costs the same (as dK/dV)
+    auto kern = bwd_dq_persist_kernel<D, CAUSAL>;
+    constexpr int smem = DqPersistCfg<D>::SMEM_BYTES;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    if (tiles <= 0) return cudaSuccess;
+    if (tiles > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+    const unsigned grid = unsigned(tiles < sm_count() ? tiles : sm_count());
+    kern<<<dim3(grid), dim3(kThreads), smem, s>>>(tq, tk, tv, tdo, tdq, a);
+    return cudaGetLastError();
+  } else if constexpr (D <= 64) {
+    (void)tdq;
+    return launch_common(bwd_dq_split_kernel<D, CAUSAL>, DqSplitCfg<D>::SMEM_BYTES, tiles, tq, tk, tv, tdo, a, s);
+  } else {
+    (void)tdq;
+    return launch_common(bwd_dq_alt_kernel<D, CAUSAL>, DqAltCfg<D>::SMEM_BYTES, tiles, tq, tk, tv, tdo, a, s);
+  }
+}
+
+// Streaming multiprocessors of the current device (cached per device).
+int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    cache[dev] = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0 ? n : 148;
+  }
+  return cache[dev];
 }
 
 template <int D, bool CAUSAL>
 cudaError_t dkdv_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tdo,
-                      const BwdArgs& a, cudaStream_t s) {
-  const long long grid = (long long)((a.N + 127) / 128) * a.Z * a.H;
-  return launch_common(bwd_dkdv_split_kernel<D, CAUSAL>, DkvSplitCfg<D>::SMEM_BYTES, grid, tq, tk, tv, tdo, a, s);
+                      const CUtensorMap& tdk, const CUtensorMap& tdv, const BwdArgs& a, cudaStream_t s) {
+  const long long tiles = (long long)((a.N + 127) / 128) * a.Z * a.H;
+  // Persistent (static round-robin) when every tile costs the same; causal tiles differ, and the
+  // hardware's dynamic CTA scheduling balances them better.
+  if constexpr (D <= 64 && !CAUSAL) {
+    auto kern = bwd_dkdv_persist_kernel<D, CAUSAL>;
+    constexpr int smem = DkvPersistCfg<D>::SMEM_BYTES;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    if (tiles <= 0) return cudaSuccess;
+    if (tiles > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+    const unsigned grid = unsigned(tiles < sm_count() ? tiles : sm_count());
+    kern<<<dim3(grid), dim3(kThreads), smem, s>>>(tq, tk, tv, tdo, tdk, tdv, a);
+    return cudaGetLastError();
+  } else {
+    (void)tdk;
+    (void)tdv;
+    return launch_common(bwd_dkdv_split_kernel<D, CAUSAL>, DkvSplitCfg<D>::SMEM_BYTES, tiles, tq, tk, tv, tdo, a, s);
+  }
 }
 
 }  // namespace
 
 void bwd_f16_box_rows(int D, bool dq_pass, int* q_rows, int* kv_rows) {
   // dQ: 128-row query tiles; key blocks of DqSplitCfg::BK rows (D <= 64) or DqAltCfg::BK rows (D = 128).
-  // dK/dV: 128-row key tiles; query blocks of DkvSplitCfg::BQ rows.
+  // dK/dV: 128-row key tiles; query blocks of DkvPersistCfg::BQ (D <= 64) or DkvSplitCfg::BQ rows.
   const bool wide = D <= 64;
   if (dq_pass) {
     *q_rows = 128;
     *kv_rows = wide ? DqSplitCfg<64>::BK : DqAltCfg<128>::BK;
   } else {
-    *q_rows = wide ? DkvSplitCfg<64>::BQ : DkvSplitCfg<128>::BQ;
+    *q_rows = wide ? DkvPersistCfg<64>::BQ : DkvSplitCfg<128>::BQ;
     *kv_rows = 128;
   }
 }
 
-#define TATTN_BWD_SWITCH(FN)                                                                  \
-  switch (D) {                                                                                \
-    case 16: return causal ? FN<16, true>(tq, tk, tv, tdo, a, s) : FN<16, false>(tq, tk, tv, tdo, a, s);   \
-    case 32: return causal ? FN<32, true>(tq, tk, tv, tdo, a, s) : FN<32, false>(tq, tk, tv, tdo, a, s);   \
-    case 64: return causal ? FN<64, true>(tq, tk, tv, tdo, a, s) : FN<64, false>(tq, tk, tv, tdo, a, s);   \
-    case 128: return causal ? FN<128, true>(tq, tk, tv, tdo, a, s) : FN<128, false>(tq, tk, tv, tdo, a, s); \
-    default: return cudaErrorInvalidValue;                                                    \
-  }
-
 cudaError_t launch_bwd_dq_f16(int D, bool causal, int tile_cfg, const CUtensorMap& tq, const CUtensorMap& tk,
-                              const CUtensorMap& tv, const CUtensorMap& tdo, const BwdArgs& a, cudaStream_t s) {
+                              const CUtensorMap& tv, const CUtensorMap& tdo, const CUtensorMap& tdq, const BwdArgs& a,
+                              cudaStream_t s) {
   (void)tile_cfg;
-  TATTN_BWD_SWITCH(dq_impl)
+  switch (D) {
+    case 16: return causal ? dq_impl<16, true>(tq, tk, tv, tdo, tdq, a, s) : dq_impl<16, false>(tq, tk, tv, tdo, tdq, a, s);
+    case 32: return causal ? dq_impl<32, true>(tq, tk, tv, tdo, tdq, a, s) : dq_impl<32, false>(tq, tk, tv, tdo, tdq, a, s);
+    case 64: return causal ? dq_impl<64, true>(tq, tk, tv, tdo, tdq, a, s) : dq_impl<64, false>(tq, tk, tv, tdo, tdq, a, s);
+    case 128: return causal ? dq_impl<128, true>(tq, tk, tv, tdo, tdq, a, s) : dq_impl<128, false>(tq, tk, tv, tdo, tdq, a, s);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 cudaError_t launch_bwd_dkdv_f16(int D, bool causal, int tile_cfg, const CUtensorMap& tq, const CUtensorMap& tk,
-                                const CUtensorMap& tv, const CUtensorMap& tdo, const BwdArgs& a, cudaStream_t s) {
+                                const CUtensorMap& tv, const CUtensorMap& tdo, const CUtensorMap& tdk,
+                                const CUtensorMap& tdv, const BwdArgs& a, cudaStream_t s) {
   (void)tile_cfg;
-  TATTN_BWD_SWITCH(dkdv_impl)
+  switch (D) {
+    case 16: return causal ? dkdv_impl<16, true>(tq, tk, tv, tdo, tdk, tdv, a, s) : dkdv_impl<16, false>(tq, tk, tv, tdo, tdk, tdv, a, s);
+    case 32: return causal ? dkdv_impl<32, true>(tq, tk, tv, tdo, tdk, tdv, a, s) : dkdv_impl<32, false>(tq, tk, tv, tdo, tdk, tdv, a, s);
+    case 64: return causal ? dkdv_impl<64, true>(tq, tk, tv, tdo, tdk, tdv, a, s) : dkdv_impl<64, false>(tq, tk, tv, tdo, tdk, tdv, a, s);
+    case 128: return causal ? dkdv_impl<128, true>(tq, tk, tv, tdo, tdk, tdv, a, s) : dkdv_impl<128, false>(tq, tk, tv, tdo, tdk, tdv, a, s);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
-#undef TATTN_BWD_SWITCH
 
 }  // namespace tattn

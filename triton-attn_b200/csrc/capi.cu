@@ -93,17 +93,19 @@ bool layout_ok(const void* p, Strides4 s, int Z, int H, int N, int D) {
   return true;
 }
 
-// [Z, H, N, D] fp16 tensor as a 4-D TMA map {D, N, H, Z}; box = {min(D, 64) columns, box_rows rows}
-// with the swizzle that matches one row chunk (32/64/128 bytes).
-int encode_f16(CUtensorMap* tm, const void* p, Strides4 s, int Z, int H, int N, int D, int box_rows) {
+// [Z, H, N, D] fp16 tensor as a 4-D TMA map {D, N, H, Z}; box = {box_cols columns (default min(D, 64)),
+// box_rows rows} with the swizzle that matches one box row (16 bytes: none; 32/64/128 bytes).
+int encode_f16(CUtensorMap* tm, const void* p, Strides4 s, int Z, int H, int N, int D, int box_rows, int box_cols = 0) {
   s = normalize(s, Z, H, N, D);
-  const int cw = D < 64 ? D : 64;
+  const int cw = box_cols > 0 ? box_cols : (D < 64 ? D : 64);
   cuuint64_t dims[4] = {cuuint64_t(D), cuuint64_t(N), cuuint64_t(H), cuuint64_t(Z)};
   cuuint64_t strides[3] = {cuuint64_t(s.n) * 2, cuuint64_t(s.h) * 2, cuuint64_t(s.z) * 2};
   cuuint32_t box[4] = {cuuint32_t(cw), cuuint32_t(box_rows), 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  const CUtensorMapSwizzle sw = cw == 64 ? CU_TENSOR_MAP_SWIZZLE_128B
-                                         : (cw == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+  const CUtensorMapSwizzle sw = cw == 64   ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : cw == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                : cw == 16 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                           : CU_TENSOR_MAP_SWIZZLE_NONE;
   CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(p), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -235,10 +237,8 @@ int bwd_common(bool dq_pass, const void* q, const void* k, const void* v, const 
   if (!layout_ok(q, a.sq, Z, H, N, D) || !layout_ok(k, a.sk, Z, H, N, D) || !layout_ok(v, a.sv, Z, H, N, D) ||
       !layout_ok(dout, a.sdo, Z, H, N, D))
     return TATTN_ERR_LAYOUT;
-  const int64_t dense_n = D;
   if ((reinterpret_cast<uintptr_t>(dq_pass ? dq : dk) & 15u) != 0 || (!dq_pass && (reinterpret_cast<uintptr_t>(dv) & 15u)))
     return TATTN_ERR_LAYOUT;
-  (void)dense_n;
   CUtensorMap tq, tk, tv, tdo;
   // dQ: query tiles of 128 rows, key blocks of 64 rows; dK/dV: key tiles of 128 rows, query blocks of 64.
   int q_rows = 0, kv_rows = 0;
@@ -247,8 +247,18 @@ int bwd_common(bool dq_pass, const void* q, const void* k, const void* v, const 
   if ((rc = encode_f16(&tk, k, a.sk, Z, H, N, D, kv_rows)) != TATTN_OK) return rc;
   if ((rc = encode_f16(&tv, v, a.sv, Z, H, N, D, kv_rows)) != TATTN_OK) return rc;
   if ((rc = encode_f16(&tdo, dout, a.sdo, Z, H, N, D, q_rows)) != TATTN_OK) return rc;
-  return cuda_rc(dq_pass ? launch_bwd_dq_f16(D, causal != 0, tile_cfg, tq, tk, tv, tdo, a, s)
-                         : launch_bwd_dkdv_f16(D, causal != 0, tile_cfg, tq, tk, tv, tdo, a, s));
+  // dQ / dK / dV are dense [Z, H, N, D]; the kernels write them through TMA store maps (dQ: each
+  // compute warpgroup stores half of the columns).
+  const Strides4 dense{int64_t(H) * N * D, int64_t(N) * D, D, 1};
+  if (dq_pass) {
+    CUtensorMap tdq;
+    if ((rc = encode_f16(&tdq, dq, dense, Z, H, N, D, kBwdStoreRows, D <= 64 ? D / 2 : 0)) != TATTN_OK) return rc;
+    return cuda_rc(launch_bwd_dq_f16(D, causal != 0, tile_cfg, tq, tk, tv, tdo, tdq, a, s));
+  }
+  CUtensorMap tdk, tdv;
+  if ((rc = encode_f16(&tdk, dk, dense, Z, H, N, D, kBwdStoreRows, D <= 64 ? D / 2 : 0)) != TATTN_OK) return rc;
+  if ((rc = encode_f16(&tdv, dv, dense, Z, H, N, D, kBwdStoreRows, D <= 64 ? D / 2 : 0)) != TATTN_OK) return rc;
+  return cuda_rc(launch_bwd_dkdv_f16(D, causal != 0, tile_cfg, tq, tk, tv, tdo, tdk, tdv, a, s));
 }
 
 }  // namespace

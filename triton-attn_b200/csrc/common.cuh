@@ -125,6 +125,28 @@ __device__ __forceinline__ void tma_load_4d(uint32_t smem_dst, const CUtensorMap
       : "memory");
 }
 
+// TMA tile store from shared memory (bulk-group completion). The source must be visible to the async
+// proxy first (fence_proxy_async_smem after the generic stores). Coordinates are never negative here.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* tm, uint32_t smem_src, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tm)),
+               "r"(smem_src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until every committed store of this thread has finished reading its shared-memory source.
+__device__ __forceinline__ void tma_store_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Wait until every committed store of this thread has completed.
+__device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Byte offset of the 16-byte unit at `byte` inside a TMA/UMMA swizzled region whose rows are SWB bytes
+// (SWB = 128, 64, 32): the unit index is XORed with address bits [7, 7 + log2(SWB/16)).
+template <int SWB>
+__device__ __forceinline__ uint32_t swizzle_offset(uint32_t byte) {
+  return byte ^ (((byte >> 7) & uint32_t(SWB / 16 - 1)) << 4);
+}
+
 // ----------------------------------------------------------------------------------------------
 // tcgen05: TMEM allocation, fences, MMA, commit
 // ----------------------------------------------------------------------------------------------

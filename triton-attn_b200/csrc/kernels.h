@@ -48,10 +48,16 @@ void bwd_f16_box_rows(int D, bool dq_pass, int* q_rows, int* kv_rows);
 // fp16 tcgen05 kernels (tensor maps describe [Z, H, N, D] tensors as 4-D {D, N, H, Z}).
 cudaError_t launch_fwd_f16(int D, bool causal, int tile_cfg, const CUtensorMap& tq, const CUtensorMap& tk,
                            const CUtensorMap& tv, const FwdArgs& a, cudaStream_t s);
+// tdq: store map of the dense dQ output, kBwdStoreRows-row boxes of D/2 columns (D <= 64).
 cudaError_t launch_bwd_dq_f16(int D, bool causal, int tile_cfg, const CUtensorMap& tq, const CUtensorMap& tk,
-                              const CUtensorMap& tv, const CUtensorMap& tdo, const BwdArgs& a, cudaStream_t s);
+                              const CUtensorMap& tv, const CUtensorMap& tdo, const CUtensorMap& tdq, const BwdArgs& a,
+                              cudaStream_t s);
+// tdk / tdv: store maps of the dense dK / dV outputs, kBwdStoreRows-row boxes of D/2 columns (D <= 64).
 cudaError_t launch_bwd_dkdv_f16(int D, bool causal, int tile_cfg, const CUtensorMap& tq, const CUtensorMap& tk,
-                                const CUtensorMap& tv, const CUtensorMap& tdo, const BwdArgs& a, cudaStream_t s);
+                                const CUtensorMap& tv, const CUtensorMap& tdo, const CUtensorMap& tdk,
+                                const CUtensorMap& tdv, const BwdArgs& a, cudaStream_t s);
+// Box height of the backward's output store maps (one warp's 32 TMEM lanes).
+constexpr int kBwdStoreRows = 32;
 
 // SIMT kernels (fp32 inputs; any strides).
 cudaError_t launch_fwd_f32(int D, bool causal, const void* q, const void* k, const void* v, Strides4 sq,
