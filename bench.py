@@ -50,7 +50,7 @@ T4_PUBLISHED = {"cfg2": 16.9, "cfg3": 15.9}  # reference fwd+bwd TF
 L2_BYTES = 126 * 2**20
 # DRAM bytes (read + write) of one launch of the dominant kernel, from the committed ncu capture
 # profiles/bwd_dkdv_cfg2.md (dram__bytes_read.sum + dram__bytes_write.sum); None for other configs.
-NCU_TRAFFIC = {("cfg2", "dkdv"): 136_381_440 + 41_013_248}
+NCU_TRAFFIC = {("cfg2", "dkdv"): 136_370_176 + 43_040_000}
 
 
 def flops(b: int, h: int, n: int, d: int, causal: bool, mode: str) -> float:
