@@ -202,6 +202,24 @@ def test_every_tile_config(kind: str) -> None:
                     _close(got, w, torch.float16, f"cfg{idx} grad")
 
 
+
+@pytest.mark.parametrize("amp,scale", [(30.0, 1e-3), (100.0, 1.2e-4), (100.0, -1.2e-4), (100.0, 5e-5)])
+def test_large_logits_small_scale(amp: float, scale: float) -> None:
+    """Logits of magnitude 1e4-1e5 under a small sm_scale (row maxima far from the softmax's usual
+    range; the backward recomputes P from S and the stored row statistics M)."""
+    shape = (1, 2, 200, 64)
+    g = torch.Generator().manual_seed(int(amp))
+    q, k = ((torch.randn(shape, generator=g) * amp).half().cuda().requires_grad_() for _ in range(2))
+    v, do = (torch.randn(shape, generator=g).half().cuda() for _ in range(2))
+    v.requires_grad_()
+    out = attention(q, k, v, sm_scale=scale)
+    out.backward(do)
+    qn, kn, vn, don = (_np(t) for t in (q, k, v, do))
+    _close(out, naive_attention(qn, kn, vn, False, scale), torch.float16, "O")
+    for t, w, key in zip((q, k, v), naive_gradients(qn, kn, vn, don, False, scale), ("dq", "dk", "dv"), strict=True):
+        _close(t.grad, w, torch.float16, key)
+
+
 # --------------------------------------------------------------------------------- full sizes
 def _torch_ref(q, k, v, do, causal, scale):
     """fp32 materialised attention + autograd on the GPU (the definition, reference.py:18-26)."""
