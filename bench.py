@@ -50,7 +50,7 @@ T4_PUBLISHED = {"cfg2": 16.9, "cfg3": 15.9}  # reference fwd+bwd TF
 L2_BYTES = 126 * 2**20
 # DRAM bytes (read + write) of one launch of the dominant kernel, from the committed ncu capture
 # profiles/bwd_dkdv_cfg2.md (dram__bytes_read.sum + dram__bytes_write.sum); None for other configs.
-NCU_TRAFFIC = {("cfg2", "dkdv"): 136_370_176 + 43_040_000}
+NCU_TRAFFIC = {("cfg2", "dkdv"): 136_370_176 + 43_040_000, ("cfg2", "bwd_fused"): 203_631_872 + 92_393_472}
 
 
 def flops(b: int, h: int, n: int, d: int, causal: bool, mode: str) -> float:
@@ -271,6 +271,12 @@ def _kernel_times(q, k, v, do, causal, scale, iters: int) -> dict:
         "dq": lambda: lib.tattn_bwd_dq(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), dq.data_ptr(),
                                        m.data_ptr(), delta.data_ptr(), st, z, h, n, d, 0, ci, scale, 0, stream),
     }  # fmt: skip
+    if not causal and d <= 64:  # the backward the API runs for these shapes: delta, fused kernel, dQ scaling
+        ws = torch.empty((z, h, n, d), device=q.device, dtype=torch.float32)
+        st5 = _lib.strides_array(q.stride(), k.stride(), v.stride(), o.stride(), do.stride())
+        calls["bwd_fused"] = lambda: lib.tattn_bwd_fused(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), dq.data_ptr(), dk.data_ptr(),
+            dv.data_ptr(), m.data_ptr(), delta.data_ptr(), ws.data_ptr(), st5, z, h, n, d, 0, ci, scale, stream)
     out = {}
     for name, fn in calls.items():
         for _ in range(3):
@@ -450,8 +456,10 @@ def run_gpu(args) -> None:
     pk = peaks()
     # GEMM FLOPs each kernel actually performs per launch (2 flops per MAC; causal halves the pairs).
     pair_flops = 2.0 * b_local * h_local * n * n * d * (0.5 if causal else 1.0)
-    kflops = {"fwd": 2 * pair_flops, "dkdv": 4 * pair_flops, "dq": 3 * pair_flops}
-    dom = max(("fwd", "dkdv", "dq"), key=lambda kk: kt[kk])
+    # bwd_fused: 5 GEMMs (S, dP, dV, dK, dQ) per pair; its time includes the delta pass and the dQ scaling.
+    kflops = {"fwd": 2 * pair_flops, "dkdv": 4 * pair_flops, "dq": 3 * pair_flops, "bwd_fused": 5 * pair_flops}
+    step_kernels = ("fwd", "bwd_fused") if "bwd_fused" in kt else ("fwd", "dkdv", "dq")  # what a step runs
+    dom = max(step_kernels, key=lambda kk: kt[kk])
     achieved = kflops[dom] / (kt[dom] * 1e-3) / 1e12
     bytes_in = 4 * b_local * h_local * n * d * 2
     if rank == 0:
@@ -494,7 +502,8 @@ def run_gpu(args) -> None:
                 "unit": "TFLOP/s",
                 "frac": round(achieved / pk["tflops"], 4),
                 "traffic": NCU_TRAFFIC.get((args.config, dom)),
-                "traffic_source": "ncu capture (profiles/bwd_dkdv_cfg2.md)" if (args.config, dom) in NCU_TRAFFIC else None,
+                "traffic_source": (f"ncu capture (profiles/{'bwd_fused' if dom == 'bwd_fused' else 'bwd_dkdv'}_cfg2.md)"
+                                   if (args.config, dom) in NCU_TRAFFIC else None),
                 "flops_per_launch": kflops[dom],
             },
             "e2e": {

@@ -86,6 +86,20 @@ TATTN_API int tattn_bwd_dq(const void* q, const void* k, const void* v, const vo
                  const float* delta, const int64_t* strides, int Z, int H, int N, int D, int dtype, int causal,
                  float sm_scale, int tile_cfg, void* stream);
 
+/* The whole backward in two kernels: delta = rowsum(dO * O) (tattn_bwd_preprocess's job) into the
+ * caller's fp32 [Z, H, N] buffer, then dQ, dK and dV in one pass in which each (key block, query
+ * block) pair's scores, P and dS are computed once; the reference's two kernels (src/tattn/kernels.py:
+ * 151-239 and 242-321, launched at api.py:122-145) each recompute S and dO V^T. dQ is accumulated by
+ * fp32 additions at L2 into dq_acc, a caller-provided dense fp32 [Z, H, N, D] workspace (16-byte
+ * aligned; zeroed here), then scaled into dq; the order of those additions varies from run to run, so
+ * dq is not bitwise reproducible (dk and dv are). strides: 20 int64 = q, k, v, o, dout each
+ * (z, h, n, d); dq, dk, dv dense [Z, H, N, D].
+ * fp16, non-causal, D <= 64 only: other requests return TATTN_ERR_UNSUPPORTED (use the three calls). */
+TATTN_API int tattn_bwd_fused(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                    void* dq, void* dk, void* dv, const float* m, float* delta, float* dq_acc,
+                    const int64_t* strides, int Z, int H, int N, int D, int dtype, int causal, float sm_scale,
+                    void* stream);
+
 /* Largest Z*H*N accepted by tattn_bwd_noalloc (its fixed fp32 row buffer: 16 MiB per GPU). */
 #define TATTN_BWD_NOALLOC_MAX_ROWS 4194304
 

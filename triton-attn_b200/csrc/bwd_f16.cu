@@ -58,6 +58,11 @@ constexpr int kThreads = 384;
 // 8*32*216 + 4*32*72 = 64512. (With 56 the issuer and staging warps spill.)
 constexpr int kComputeRegs = 216;
 constexpr int kProducerRegs = 72;
+// The fused backward's issuer warps hold more descriptors (dS^T as two operands, K for dQ) and need
+// more than 72 registers; its compute warps fit in 208. Both splits use the whole 384 x 168 pool.
+constexpr int kFusedComputeRegs = 208;
+constexpr int kFusedProducerRegs = 88;
+static_assert(256 * kFusedComputeRegs + 128 * kFusedProducerRegs == 384 * 168, "register split");
 constexpr int kTmaWarp = 8, kMmaSWarp = 9, kMmaAccWarp = 10, kAllocWarp = 11;
 constexpr unsigned long long kDrainNs = 100ull * 1000ull * 1000ull;
 
@@ -1627,6 +1632,457 @@ cudaError_t dkdv_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtens
   }
 }
 
+// ------------------------------------------------------------------- fused backward, D <= 64
+// dK, dV and dQ in one pass over each (key tile, query block) pair, so S^T, dP^T and the exponentials
+// are computed once instead of once per output kernel (the reference's split, kernels.py:151-321,
+// recomputes QK^T and dO V^T for dQ). The persistent dK/dV structure (one CTA per SM, 128-key tiles,
+// static round-robin, ring of Q/dO blocks; K double-buffered because the dQ MMAs read it to the end of
+// a tile, V single-buffered and loaded by warp 11 once the tile's last dP^T MMA has read it) plus:
+//   * dS^T goes to shared memory ([128 keys, 128 queries] fp16, 128-byte swizzle, two 64-query
+//     chunks) instead of TMEM. The same bytes are the K-major A operand of dK += dS^T Q and the
+//     MN-major A operand of dQ_part = dS K (rows = keys, 128 contiguous bytes = 64 queries).
+//   * dQ_part of a block (128 queries x D, fp32) is accumulated in TMEM by its own MMAs; the compute
+//     warps read it one block later, right after handing over the next block's P^T/dS^T (the dQ MMAs
+//     of that block wait for the read: dq_read), and add it into a dense fp32 workspace through TMA
+//     tensor reduce-adds (32 rows x D/2 columns per warp). A second kernel scales the workspace by
+//     sm_scale into the fp16 dQ.
+// TMEM: S^T [128] | dP^T [128] | P^T [64] | dV [D] | dK [D] | dQ_part [D].
+template <int D>
+struct FusedCfg {
+  using G = Geo<D>;
+  static_assert(D <= 64, "fused backward: TMEM holds S^T, dP^T, P^T, dV, dK and the dQ partial");
+  static constexpr int BQ = 128, H = 64;
+  static constexpr int NS = 3;                            // Q/dO ring stages
+  static constexpr int T_KEY = G::tile(128);
+  static constexpr int T_Q = G::tile(BQ);
+  static constexpr int T_DS = Geo<128>::tile(128);        // dS^T [128 keys, 128 queries] fp16
+  static constexpr int DS_CHUNK = Geo<128>::chunk(128);   // 64 queries of every key row
+  static constexpr int HW = D / 2;                        // output columns per warpgroup
+  static constexpr int SWB_O = HW * 2;                    // dK/dV staging row bytes (fp16)
+  static constexpr int SWB_Q = HW * 4;                    // dQ staging row bytes (fp32)
+  static constexpr int STG_ROW = SWB_O > SWB_Q ? SWB_O : SWB_Q;
+  static constexpr int STG = 32 * STG_ROW < 1024 ? 1024 : 32 * STG_ROW;  // per-warp staging, both uses
+  static constexpr int OFF_K = 0;                         // [2 buffers] key tiles
+  static constexpr int OFF_V = 2 * T_KEY;                 // value tile
+  static constexpr int OFF_Q = 3 * T_KEY;                 // NS query blocks
+  static constexpr int OFF_DO = OFF_Q + NS * T_Q;         // NS dO blocks
+  static constexpr int OFF_DS = OFF_DO + NS * T_Q;        // dS^T of the current block
+  static constexpr int OFF_STG = OFF_DS + T_DS;           // 8 compute warps x STG
+  static constexpr int OFF_MD = OFF_STG + 8 * STG;        // NS x (BQ -M | BQ -delta) fp32
+  static constexpr int OFF_BAR = OFF_MD + NS * 2 * BQ * 4;
+  // k_full[2], k_empty[2], q_full[NS], md_full[NS], q_empty[NS], s_full, s_free, p_full, acc_free,
+  // acc_done, acc_read, fin[3], dq_read, v_full, v_empty
+  static constexpr int NBARS = 4 + 3 * NS + 12;
+  static constexpr int OFF_MISC = OFF_BAR + NBARS * 8;
+  static constexpr int SMEM_USED = OFF_MISC + 16;
+  static constexpr int SMEM_BYTES = (SMEM_USED > 118784 ? SMEM_USED : 118784) + 1024;
+  static constexpr uint32_t T_ST = 0, T_DPT = 128, T_PT = 256, T_DV = 320, T_DK = 320 + D, T_DQ = 320 + 2 * D;
+  static_assert(T_DQ + D <= 512, "TMEM budget");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+  static_assert(OFF_DS % 1024 == 0 && OFF_STG % 1024 == 0, "alignment");
+  static constexpr uint32_t IDESC_S = idesc_f16_f32(128, BQ, false);
+  static constexpr uint32_t IDESC_ACC = idesc_f16_f32(128, D, true);     // A K-major, B MN-major
+  static constexpr uint32_t IDESC_DQ = idesc_f16_f32_amn(128, D, true);  // A (dS) and B (K) MN-major
+};
+
+// Add the warp's part of a block's dQ partial (32 query rows x D/2 fp32 columns, in registers) into the
+// fp32 workspace at (col, row) through the warp's staging area.
+template <int D>
+__device__ __forceinline__ void fused_dq_out(const uint32_t* o, uint32_t stg, const CUtensorMap* tm, int col, int row,
+                                             int hi, int zi, int lane) {
+  using C = FusedCfg<D>;
+  if (lane == 0) tma_store_wait_read_all();  // the warp's previous reduce / store has read its staging
+  __syncwarp();
+#pragma unroll
+  for (int u = 0; u < C::SWB_Q / 16; ++u) {
+    const uint32_t addr = stg + swizzle_offset<C::SWB_Q>(uint32_t(lane * C::SWB_Q + u * 16));
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(o[4 * u]), "r"(o[4 * u + 1]),
+                 "r"(o[4 * u + 2]), "r"(o[4 * u + 3]) : "memory");
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {  // rows past N are clipped by the tensor map
+    tma_reduce_add_4d(tm, stg, col, row, hi, zi);
+    tma_store_commit();
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                     const __grid_constant__ CUtensorMap tm_dk, const __grid_constant__ CUtensorMap tm_dv,
+                     const __grid_constant__ CUtensorMap tm_dqacc, const BwdArgs args) {
+  using C = FusedCfg<D>;
+  using G = Geo<D>;
+  constexpr int H = C::H, BQ = C::BQ, NS = C::NS;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base_u32 - raw_u32);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* bar_kv_full = bars;                 // [2] key buffer landed
+  uint64_t* bar_kv_empty = bars + 2;            // [2] every S^T and dQ MMA of the buffer's tile has completed
+  uint64_t* bar_q_full = bars + 4;              // [NS]
+  uint64_t* bar_md_full = bars + 4 + NS;        // [NS]
+  uint64_t* bar_q_empty = bars + 4 + 2 * NS;    // [NS]
+  uint64_t* bar_s_full = bars + 4 + 3 * NS;
+  uint64_t* bar_s_free = bar_s_full + 1;
+  uint64_t* bar_p_full = bar_s_full + 2;        // P^T in TMEM and dS^T in shared memory
+  uint64_t* bar_acc_free = bar_s_full + 3;      // the block's dV, dK and dQ MMAs completed
+  uint64_t* bar_acc_done = bar_s_full + 4;
+  uint64_t* bar_acc_read = bar_s_full + 5;      // the compute warps hold the tile's dV/dK and last dQ part
+  uint64_t* bar_fin = bar_s_full + 6;           // [3]
+  uint64_t* bar_dq_read = bar_s_full + 9;       // the compute warps hold the previous block's dQ part
+  uint64_t* bar_v_full = bar_s_full + 10;       // value tile landed
+  uint64_t* bar_v_empty = bar_s_full + 11;      // every dP^T MMA of the value tile's tile has completed
+  float* md = reinterpret_cast<float*>(smem + C::OFF_MD);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+  const CtaAbort ab{abort_flag, args.status};
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int N = args.N;
+  const int zh = args.Z * args.H;
+  const int nct = (N + 127) / 128;
+  const int ntiles = nct * zh;
+  const int n = (N + BQ - 1) / BQ;  // query blocks of every tile (non-causal)
+
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bar_kv_full[b], 1);
+      mbar_init(&bar_kv_empty[b], 2);  // S^T/dP^T issuer + dV/dK/dQ issuer (which reads K for dQ)
+    }
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&bar_q_full[s], 1);
+      mbar_init(&bar_md_full[s], 32);
+      mbar_init(&bar_q_empty[s], 2);
+    }
+    mbar_init(bar_s_full, 1);
+    mbar_init(bar_s_free, 256);
+    mbar_init(bar_p_full, 256);
+    mbar_init(bar_acc_free, 1);
+    mbar_init(bar_acc_done, 1);
+    mbar_init(bar_acc_read, 256);
+    for (int i = 0; i < 3; ++i) mbar_init(&bar_fin[i], 1);
+    mbar_init(bar_dq_read, 256);
+    mbar_init(bar_v_full, 1);
+    mbar_init(bar_v_empty, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kAllocWarp) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  if (warp == kTmaWarp && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+    tma_prefetch_desc(&tm_do);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sK = base_u32 + C::OFF_K, sV = base_u32 + C::OFF_V;
+  const uint32_t sQ = base_u32 + C::OFF_Q, sDO = base_u32 + C::OFF_DO;
+  const uint32_t sDS = base_u32 + C::OFF_DS;
+
+  if (warp >= kTmaWarp) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kFusedProducerRegs));
+    if (warp == kTmaWarp) {
+      // -------------------------------------------------------------- TMA producer + -M/-delta staging
+      int g = 0, it = 0, kv_issued = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
+        int bh, kt;
+        dkdv_tile(tile, nct, zh, false, &bh, &kt);
+        const int zi = bh / args.H, hi = bh % args.H, k0 = 128 * kt;
+        const int kb = it & 1;
+        if (it >= 2 && !warp_wait(&bar_kv_empty[kb], ((it >> 1) - 1) & 1, ab)) { ok = false; break; }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&bar_kv_full[kb], C::T_KEY);
+          for (int ch = 0; ch < G::NCH; ++ch)
+            tma_load_4d(sK + kb * C::T_KEY + ch * G::chunk(128), &tm_k, ch * G::CW, k0, hi, zi, &bar_kv_full[kb]);
+        }
+        ++kv_issued;
+        const float* mrow = args.m + int64_t(bh) * N;
+        const float* drow = args.delta + int64_t(bh) * N;
+        for (int c = 0; c < n; ++c, ++g) {
+          const int st = g % NS;
+          if (g >= NS && !warp_wait(&bar_q_empty[st], ((g / NS) - 1) & 1, ab)) { ok = false; break; }
+          const int qr = c * BQ;
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&bar_q_full[st], 2 * C::T_Q);
+            for (int ch = 0; ch < G::NCH; ++ch) {
+              tma_load_4d(sQ + st * C::T_Q + ch * G::chunk(BQ), &tm_q, ch * G::CW, qr, hi, zi, &bar_q_full[st]);
+              tma_load_4d(sDO + st * C::T_Q + ch * G::chunk(BQ), &tm_do, ch * G::CW, qr, hi, zi, &bar_q_full[st]);
+            }
+          }
+          float* slot = md + st * 2 * BQ;
+#pragma unroll
+          for (int j = lane; j < BQ; j += 32) {
+            const int q = qr + j;
+            slot[j] = q < N ? -mrow[q] : 0.f;
+            slot[BQ + j] = q < N ? -drow[q] : 0.f;
+          }
+          mbar_arrive(&bar_md_full[st]);
+        }
+      }
+      // Every copy issued must land before the CTA exits (instant on the normal path).
+      if (lane == 0) {
+        for (int ii = max(0, kv_issued - 2); ii < kv_issued; ++ii) mbar_drain(&bar_kv_full[ii & 1], (ii >> 1) & 1, kDrainNs);
+        for (int gg = max(0, g - NS); gg < g; ++gg) mbar_drain(&bar_q_full[gg % NS], (gg / NS) & 1, kDrainNs);
+      }
+    } else if (warp == kMmaSWarp) {
+      // -------------------------------------------------------------- S^T/dP^T issuer
+      const uint32_t idesc_s = C::IDESC_S | (args.negate_s ? (1u << 13) : 0u);
+      const uint64_t dK = smem_desc(sK, 16, 8 * G::SWB, G::LAYOUT);
+      const uint64_t dV = smem_desc(sV, 16, 8 * G::SWB, G::LAYOUT);
+      const uint64_t dQ = smem_desc(sQ, 16, 8 * G::SWB, G::LAYOUT);
+      const uint64_t dDO = smem_desc(sDO, 16, 8 * G::SWB, G::LAYOUT);
+      int g = 0, it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
+        const int kb = it & 1;
+        if (!warp_wait(&bar_kv_full[kb], (it >> 1) & 1, ab) || !warp_wait(bar_v_full, it & 1, ab)) {
+          ok = false;
+          break;
+        }
+        const uint64_t ko = uint64_t((kb * C::T_KEY) >> 4);
+        for (int c = 0; c < n; ++c, ++g) {
+          if (g > 0 && !warp_wait(bar_s_free, (g - 1) & 1, ab)) { ok = false; break; }
+          if (!warp_wait(&bar_q_full[g % NS], (g / NS) & 1, ab)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t so = uint64_t(((g % NS) * C::T_Q) >> 4);
+          mma_kmajor<D, G::chunk(128), G::chunk(BQ)>(tmem + C::T_ST, dK + ko, dQ + so, idesc_s);
+          mma_kmajor<D, G::chunk(128), G::chunk(BQ)>(tmem + C::T_DPT, dV, dDO + so, C::IDESC_S);
+          mma_commit_elect(bar_s_full);
+          mma_commit_elect(&bar_q_empty[g % NS]);
+        }
+        mma_commit_elect(&bar_kv_empty[kb]);
+        mma_commit_elect(bar_v_empty);
+      }
+      mma_commit_elect(&bar_fin[0]);
+      mbar_drain(&bar_fin[0], 0, kDrainNs);
+    } else if (warp == kMmaAccWarp) {
+      // -------------------------------------------------------------- dV / dK / dQ issuer
+      const uint64_t dQmn = smem_desc(sQ, G::chunk(BQ), 8 * G::SWB, G::LAYOUT);
+      const uint64_t dDOmn = smem_desc(sDO, G::chunk(BQ), 8 * G::SWB, G::LAYOUT);
+      const uint64_t dKmn = smem_desc(sK, G::chunk(128), 8 * G::SWB, G::LAYOUT);
+      const uint64_t dDSk = smem_desc(sDS, 16, 1024, 2u);                // dS^T as K-major A (dK)
+      const uint64_t dDSmn = smem_desc(sDS, C::DS_CHUNK, 1024, 2u);      // dS as MN-major A (dQ)
+      int g = 0, it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
+        const int kb = it & 1;
+        const uint64_t ko = uint64_t((kb * C::T_KEY) >> 4);
+        // The accumulators are overwritten by this tile's first MMAs: the previous tile's epilogue
+        // must have read them (and the previous tile's last dQ part).
+        if (it > 0 && !warp_wait(bar_acc_read, (it - 1) & 1, ab)) { ok = false; break; }
+        if (!warp_wait(&bar_kv_full[kb], (it >> 1) & 1, ab)) { ok = false; break; }  // K for the dQ MMAs
+        for (int c = 0; c < n; ++c, ++g) {
+          if (!warp_wait(bar_p_full, g & 1, ab) || !warp_wait(&bar_q_full[g % NS], (g / NS) & 1, ab)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t so = uint64_t(((g % NS) * C::T_Q) >> 4);
+          const uint32_t acc = c > 0 ? 1u : 0u;
+          // dV += P^T dO (A = P^T from TMEM)
+          mma_tmem_mn<D, BQ / 16>(tmem + C::T_DV, tmem + C::T_PT, dDOmn + so, C::IDESC_ACC, acc);
+          // dK += dS^T Q (A = dS^T, K-major over queries: 64-query chunks, 32 bytes per K step)
+#pragma unroll
+          for (int kk = 0; kk < BQ / 16; ++kk)
+            mma_f16_ss_elect(tmem + C::T_DK, dDSk + uint64_t(((kk / 4) * C::DS_CHUNK + (kk % 4) * 32) >> 4),
+                             dQmn + so + uint64_t((kk * 16 * G::SWB) >> 4), C::IDESC_ACC, kk > 0 ? 1u : acc);
+          // dQ_part = dS K (A = dS, MN-major: 16 key rows of 128 bytes per K step; B = K, MN-major), once
+          // the compute warps hold the previous block's dQ part.
+          if (!warp_wait(bar_dq_read, g & 1, ab)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 128 / 16; ++kk)
+            mma_f16_ss_elect(tmem + C::T_DQ, dDSmn + uint64_t((kk * 16 * 128) >> 4),
+                             dKmn + ko + uint64_t((kk * 16 * G::SWB) >> 4), C::IDESC_DQ, kk > 0 ? 1u : 0u);
+          mma_commit_elect(bar_acc_free);
+          mma_commit_elect(&bar_q_empty[g % NS]);
+        }
+        if (ok) {
+          mma_commit_elect(bar_acc_done);
+          mma_commit_elect(&bar_kv_empty[kb]);  // the tile's dQ MMAs have read its K buffer
+        }
+      }
+      mma_commit_elect(&bar_fin[2]);
+      mbar_drain(&bar_fin[2], 0, kDrainNs);
+    } else {
+      // -------------------------------------------------------------- value tiles (warp 11)
+      int it = 0, v_issued = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
+        int bh, kt;
+        dkdv_tile(tile, nct, zh, false, &bh, &kt);
+        if (it >= 1 && !warp_wait(bar_v_empty, (it - 1) & 1, ab)) { ok = false; break; }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(bar_v_full, C::T_KEY);
+          for (int ch = 0; ch < G::NCH; ++ch)
+            tma_load_4d(sV + ch * G::chunk(128), &tm_v, ch * G::CW, 128 * kt, bh % args.H, bh / args.H, bar_v_full);
+        }
+        ++v_issued;
+      }
+      if (lane == 0 && v_issued > 0) mbar_drain(bar_v_full, (v_issued - 1) & 1, kDrainNs);
+    }
+  } else {
+    // ------------------------------------------------------------------ compute warpgroups
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kFusedComputeRegs));
+    const int w = warp / 4;            // query half of every block; writes dV (0) or dK (1)
+    const int r = threadIdx.x % 128;   // key row within the tile = TMEM lane
+    const int q4 = warp % 4;           // TMEM lane quadrant: rows [32 q4, 32 q4 + 32)
+    const uint32_t tl = tmem + (uint32_t(q4 * 32) << 16);
+    const uint32_t stg = base_u32 + C::OFF_STG + warp * C::STG;
+    // This thread's row of dS^T: key r, queries [64 w, 64 w + 64) = one 128-byte row of chunk w.
+    const uint32_t ds_row = sDS + w * C::DS_CHUNK + r * 128;
+    const uint64_t scale2 = f2(args.qk_scale, args.qk_scale);
+    const CUtensorMap* tm_out = w ? &tm_dk : &tm_dv;
+    const float mul = w ? args.sm_scale : 1.f;
+    int g = 0, it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
+      int bh, kt;
+      dkdv_tile(tile, nct, zh, false, &bh, &kt);
+      const int zi = bh / args.H, hi = bh % args.H, k0 = 128 * kt;
+      const int key = k0 + r;
+      for (int c = 0; c < n; ++c, ++g) {
+        const int st = g % NS;
+        if (!warp_wait(bar_s_full, g & 1, ab)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t s[H], dp[H];
+        tmem_load_cols<H>(tl + C::T_ST + w * H, s);
+        tmem_load_cols<H>(tl + C::T_DPT + w * H, dp);
+        tmem_wait_ld();
+        reg_fence<H>(s);
+        reg_fence<H>(dp);
+        tc_fence_before();
+        mbar_arrive(bar_s_free);  // the tensor core may now write S^T/dP^T of the next block
+        if (!warp_wait(&bar_md_full[st], (g / NS) & 1, ab)) { ok = false; break; }
+        const float* mq = md + st * 2 * BQ + w * H;
+        const int q0 = c * BQ + w * H;  // first query column of this warpgroup's half
+        const bool masked = (q0 + H > N) || (k0 + 128 > N);
+        const int c_hi = key < N ? N - q0 : 0;  // valid query columns: c < c_hi
+        uint32_t pt[H / 2], dst[H / 2];
+        if (masked)
+          pds_row<H, true>(s, dp, mq, mq + BQ, pt, dst, scale2, 0, c_hi);
+        else
+          pds_row<H, false>(s, dp, mq, mq + BQ, pt, dst, scale2, 0, c_hi);
+        if (g > 0) {  // the previous block's dV/dK/dQ MMAs have read P^T and dS^T and written dQ_part
+          if (!warp_wait(bar_acc_free, (g - 1) & 1, ab)) { ok = false; break; }
+          tc_fence_after();
+        }
+        tmem_store_cols<H / 2>(tl + C::T_PT + w * (H / 2), pt);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const uint32_t addr = ds_row + uint32_t((u ^ (r & 7)) << 4);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(dst[4 * u]), "r"(dst[4 * u + 1]),
+                       "r"(dst[4 * u + 2]), "r"(dst[4 * u + 3]) : "memory");
+        }
+        fence_proxy_async_smem();  // the tensor core reads dS^T through the async proxy
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar_p_full);
+        // The previous block's dQ part (the last block of a tile leaves in the epilogue): into registers,
+        // release the accumulator to this block's dQ MMAs, then add it into the workspace.
+        if (c > 0) {
+          uint32_t oq[C::HW];
+          tmem_load_cols<C::HW>(tl + C::T_DQ + w * C::HW, oq);
+          tmem_wait_ld();
+          reg_fence<C::HW>(oq);
+          tc_fence_before();
+          mbar_arrive(bar_dq_read);
+          fused_dq_out<D>(oq, stg, &tm_dqacc, w * C::HW, (c - 1) * BQ + 32 * q4, hi, zi, lane);
+        } else {
+          mbar_arrive(bar_dq_read);
+        }
+      }
+      if (!ok || !warp_wait(bar_acc_done, it & 1, ab)) { ok = false; break; }
+      // ---- epilogue: the last block's dQ part, then dV (warpgroup 0) or dK * sm_scale (warpgroup 1)
+      tc_fence_after();
+      uint32_t o[D];
+      tmem_load_cols<D>(tl + (w ? C::T_DK : C::T_DV), o);
+      uint32_t oq[C::HW];
+      tmem_load_cols<C::HW>(tl + C::T_DQ + w * C::HW, oq);
+      tmem_wait_ld();
+      reg_fence<D>(o);
+      reg_fence<C::HW>(oq);
+      tc_fence_before();
+      mbar_arrive(bar_acc_read);  // the next tile's first MMAs may overwrite the accumulators
+      fused_dq_out<D>(oq, stg, &tm_dqacc, w * C::HW, (n - 1) * BQ + 32 * q4, hi, zi, lane);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {  // columns [half * HW, half * HW + HW)
+        if (lane == 0) tma_store_wait_read_all();  // this warp's previous store has left the staging area
+        __syncwarp();
+#pragma unroll
+        for (int u = 0; u < C::SWB_O / 16; ++u) {
+          const int cc = half * C::HW + u * 8;
+          const uint32_t addr = stg + swizzle_offset<C::SWB_O>(uint32_t(lane * C::SWB_O + u * 16));
+          const uint32_t h0 = pack_half2(__uint_as_float(o[cc + 0]) * mul, __uint_as_float(o[cc + 1]) * mul);
+          const uint32_t h1 = pack_half2(__uint_as_float(o[cc + 2]) * mul, __uint_as_float(o[cc + 3]) * mul);
+          const uint32_t h2 = pack_half2(__uint_as_float(o[cc + 4]) * mul, __uint_as_float(o[cc + 5]) * mul);
+          const uint32_t h3 = pack_half2(__uint_as_float(o[cc + 6]) * mul, __uint_as_float(o[cc + 7]) * mul);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(h0), "r"(h1), "r"(h2), "r"(h3)
+                       : "memory");
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {  // rows past N are clipped by the tensor map
+          tma_store_4d(tm_out, stg, half * C::HW, k0 + 32 * q4, hi, zi);
+          tma_store_commit();
+        }
+      }
+    }
+    if (lane == 0) tma_store_wait_all();  // staging must stay valid until the stores and reduces are done
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kAllocWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// dq = sm_scale * acc (dense [Z, H, N, D]; fp32 workspace to fp16), 8 elements per thread.
+__global__ void __launch_bounds__(256) dq_convert_kernel(const float4* __restrict__ acc, uint4* __restrict__ dq,
+                                                         long long n8, float scale) {
+  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < n8; i += (long long)gridDim.x * 256) {
+    const float4 a = acc[2 * i], b = acc[2 * i + 1];
+    dq[i] = make_uint4(pack_half2(a.x * scale, a.y * scale), pack_half2(a.z * scale, a.w * scale),
+                       pack_half2(b.x * scale, b.y * scale), pack_half2(b.z * scale, b.w * scale));
+  }
+}
+
+template <int D>
+cudaError_t fused_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tdo,
+                       const CUtensorMap& tdk, const CUtensorMap& tdv, const CUtensorMap& tdqacc, const BwdArgs& a,
+                       float* dq_acc, cudaStream_t s) {
+  auto kern = bwd_fused_kernel<D>;
+  constexpr int smem = FusedCfg<D>::SMEM_BYTES;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  const long long tiles = (long long)((a.N + 127) / 128) * a.Z * a.H;
+  if (tiles <= 0) return cudaSuccess;
+  if (tiles > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+  const long long count = (long long)a.Z * a.H * a.N * D;
+  const unsigned grid = unsigned(tiles < sm_count() ? tiles : sm_count());
+  kern<<<dim3(grid), dim3(kThreads), smem, s>>>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  const long long n8 = count / 8;  // D is a multiple of 8
+  const unsigned cgrid = unsigned(n8 / 256 + 1 < 4LL * sm_count() ? n8 / 256 + 1 : 4LL * sm_count());
+  dq_convert_kernel<<<cgrid, 256, 0, s>>>(reinterpret_cast<const float4*>(dq_acc), reinterpret_cast<uint4*>(a.dq),
+                                          n8, a.sm_scale);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 void bwd_f16_box_rows(int D, bool dq_pass, int* q_rows, int* kv_rows) {
@@ -1665,6 +2121,19 @@ cudaError_t launch_bwd_dkdv_f16(int D, bool causal, int tile_cfg, const CUtensor
     case 64: return causal ? dkdv_impl<64, true>(tq, tk, tv, tdo, tdk, tdv, a, s) : dkdv_impl<64, false>(tq, tk, tv, tdo, tdk, tdv, a, s);
     case 128: return causal ? dkdv_impl<128, true>(tq, tk, tv, tdo, tdk, tdv, a, s) : dkdv_impl<128, false>(tq, tk, tv, tdo, tdk, tdv, a, s);
     default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_bwd_fused_f16(int D, bool causal, const CUtensorMap& tq, const CUtensorMap& tk,
+                                 const CUtensorMap& tv, const CUtensorMap& tdo, const CUtensorMap& tdk,
+                                 const CUtensorMap& tdv, const CUtensorMap& tdqacc, const BwdArgs& a, float* dq_acc,
+                                 cudaStream_t s) {
+  if (causal) return cudaErrorNotSupported;
+  switch (D) {
+    case 16: return fused_impl<16>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s);
+    case 32: return fused_impl<32>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s);
+    case 64: return fused_impl<64>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s);
+    default: return cudaErrorNotSupported;
   }
 }
 

@@ -112,6 +112,24 @@ int encode_f16(CUtensorMap* tm, const void* p, Strides4 s, int Z, int H, int N, 
   return r == CUDA_SUCCESS ? TATTN_OK : TATTN_ERR_LAYOUT;
 }
 
+// Dense [Z, H, N, D] fp32 tensor as a 4-D TMA map {D, N, H, Z} with boxes of box_cols x box_rows and
+// the swizzle of one box row (box_cols * 4 bytes: 32, 64 or 128).
+int encode_f32_dense(CUtensorMap* tm, void* p, int Z, int H, int N, int D, int box_rows, int box_cols) {
+  cuuint64_t dims[4] = {cuuint64_t(D), cuuint64_t(N), cuuint64_t(H), cuuint64_t(Z)};
+  cuuint64_t strides[3] = {cuuint64_t(D) * 4, cuuint64_t(N) * D * 4, cuuint64_t(H) * N * D * 4};
+  cuuint32_t box[4] = {cuuint32_t(box_cols), cuuint32_t(box_rows), 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const int row_bytes = box_cols * 4;
+  const CUtensorMapSwizzle sw = row_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : row_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                : row_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                  : CU_TENSOR_MAP_SWIZZLE_NONE;
+  CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? TATTN_OK : TATTN_ERR_LAYOUT;
+}
+
 int cuda_rc(cudaError_t e) {
   if (e == cudaSuccess) return TATTN_OK;
   if (e == cudaErrorNotSupported) return TATTN_ERR_UNSUPPORTED;
@@ -275,6 +293,63 @@ extern "C" int tattn_bwd_dq(const void* q, const void* k, const void* v, const v
                             int dtype, int causal, float sm_scale, int tile_cfg, void* stream) {
   return bwd_common(true, q, k, v, dout, dq, nullptr, nullptr, m, delta, strides, Z, H, N, D, dtype, causal,
                     sm_scale, tile_cfg, stream);
+}
+
+extern "C" int tattn_bwd_fused(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                               void* dq, void* dk, void* dv, const float* m, float* delta, float* dq_acc,
+                               const int64_t* strides, int Z, int H, int N, int D, int dtype, int causal,
+                               float sm_scale, void* stream) {
+  if (!strides || !valid_dims(Z, H, N, D) || (dtype != TATTN_F16 && dtype != TATTN_F32))
+    return TATTN_ERR_INVALID_ARGUMENT;
+  if (dtype != TATTN_F16 || causal || D > 64) return TATTN_ERR_UNSUPPORTED;
+  if (int64_t(Z) * H * N == 0) return TATTN_OK;
+  if (!q || !k || !v || !o || !dout || !dq || !dk || !dv || !m || !delta || !dq_acc) return TATTN_ERR_INVALID_ARGUMENT;
+  DeviceState* st;
+  int rc = device_setup(&st);
+  if (rc != TATTN_OK) return rc;
+  BwdArgs a{};
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.o = o;
+  a.dout = dout;
+  a.sq = load_strides(strides);
+  a.sk = load_strides(strides + 4);
+  a.sv = load_strides(strides + 8);
+  a.so = load_strides(strides + 12);
+  a.sdo = load_strides(strides + 16);
+  a.m = m;
+  a.delta = delta;
+  a.dq = dq;
+  a.dk = dk;
+  a.dv = dv;
+  a.dq_acc = dq_acc;
+  a.Z = Z;
+  a.H = H;
+  a.N = N;
+  a.sm_scale = sm_scale;
+  a.qk_scale = (sm_scale < 0.f ? -sm_scale : sm_scale) * kLog2e;
+  a.negate_s = sm_scale < 0.f ? 1 : 0;
+  a.status = st->status;
+  if (!layout_ok(q, a.sq, Z, H, N, D) || !layout_ok(k, a.sk, Z, H, N, D) || !layout_ok(v, a.sv, Z, H, N, D) ||
+      !layout_ok(o, a.so, Z, H, N, D) || !layout_ok(dout, a.sdo, Z, H, N, D))
+    return TATTN_ERR_LAYOUT;
+  for (const void* p : {static_cast<const void*>(dq), static_cast<const void*>(dk), static_cast<const void*>(dv),
+                        static_cast<const void*>(dq_acc)})
+    if ((reinterpret_cast<uintptr_t>(p) & 15u) != 0) return TATTN_ERR_LAYOUT;
+  CUtensorMap tq, tk, tv, tdo, tdk, tdv, tdqacc;
+  // Key tiles and query blocks of 128 rows.
+  if ((rc = encode_f16(&tq, q, a.sq, Z, H, N, D, 128)) != TATTN_OK) return rc;
+  if ((rc = encode_f16(&tk, k, a.sk, Z, H, N, D, 128)) != TATTN_OK) return rc;
+  if ((rc = encode_f16(&tv, v, a.sv, Z, H, N, D, 128)) != TATTN_OK) return rc;
+  if ((rc = encode_f16(&tdo, dout, a.sdo, Z, H, N, D, 128)) != TATTN_OK) return rc;
+  const Strides4 dense{int64_t(H) * N * D, int64_t(N) * D, D, 1};
+  if ((rc = encode_f16(&tdk, dk, dense, Z, H, N, D, kBwdStoreRows, D / 2)) != TATTN_OK) return rc;
+  if ((rc = encode_f16(&tdv, dv, dense, Z, H, N, D, kBwdStoreRows, D / 2)) != TATTN_OK) return rc;
+  if ((rc = encode_f32_dense(&tdqacc, dq_acc, Z, H, N, D, kBwdStoreRows, D / 2)) != TATTN_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((rc = cuda_rc(launch_bwd_preprocess(D, true, a, s))) != TATTN_OK) return rc;  // delta, zeroed dq_acc
+  return cuda_rc(launch_bwd_fused_f16(D, causal != 0, tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s));
 }
 
 extern "C" int tattn_layout_ok(const void* ptr, const int64_t* strides, int Z, int H, int N, int D) {

@@ -133,6 +133,15 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap* tm, uint32_t sme
                "r"(smem_src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
                : "memory");
 }
+// Element-wise add of a shared-memory box into global memory (the tensor map's element type, here fp32),
+// performed at L2; completes through the same bulk groups as the stores.
+__device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* tm, uint32_t smem_src, int c0, int c1, int c2,
+                                                  int c3) {
+  asm volatile("cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tm)),
+               "r"(smem_src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
 __device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until every committed store of this thread has finished reading its shared-memory source.
 __device__ __forceinline__ void tma_store_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
@@ -235,6 +244,10 @@ __device__ __forceinline__ void mma_commit_elect(uint64_t* bar) {
 //   15 A major (0 = K), 16 B major (1 = MN), 17-22 N>>3, 24-28 M>>4.
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, bool b_mn_major) {
   return (1u << 4) | (b_mn_major ? (1u << 16) : 0u) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
+// The same with the A operand MN-major (transposed: M contiguous in shared memory) as well.
+__host__ __device__ constexpr uint32_t idesc_f16_f32_amn(int M, int N, bool b_mn_major) {
+  return idesc_f16_f32(M, N, b_mn_major) | (1u << 15);
 }
 
 // Shared-memory matrix descriptor (sm100 version field = 1).

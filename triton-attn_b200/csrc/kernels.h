@@ -31,6 +31,7 @@ struct BwdArgs {
   float* delta;      // [Z, H, N]: rowsum(dO * O)
   // outputs (dense [Z, H, N, D])
   void* dq; void* dk; void* dv;
+  float* dq_acc;     // fused backward: dense fp32 [Z, H, N, D] dQ workspace (zeroed by the preprocess), or null
   int Z, H, N;
   float sm_scale;    // signed
   float qk_scale;    // |sm_scale| * log2(e)
@@ -56,6 +57,15 @@ cudaError_t launch_bwd_dq_f16(int D, bool causal, int tile_cfg, const CUtensorMa
 cudaError_t launch_bwd_dkdv_f16(int D, bool causal, int tile_cfg, const CUtensorMap& tq, const CUtensorMap& tk,
                                 const CUtensorMap& tv, const CUtensorMap& tdo, const CUtensorMap& tdk,
                                 const CUtensorMap& tdv, const BwdArgs& a, cudaStream_t s);
+// Fused backward (dK, dV and dQ in one kernel; non-causal, D <= 64): tq/tdo with 128-row boxes, tk/tv
+// 128-row boxes, tdk/tdv store maps as above, tdqacc a reduce map over the dense fp32 workspace dq_acc
+// [Z, H, N, D] (kBwdStoreRows-row boxes of D/2 columns), zeroed beforehand (launch_bwd_preprocess with
+// a.dq_acc set). Runs the kernel, then writes a.dq = sm_scale * dq_acc as fp16. cudaErrorNotSupported
+// for other shapes.
+cudaError_t launch_bwd_fused_f16(int D, bool causal, const CUtensorMap& tq, const CUtensorMap& tk,
+                                 const CUtensorMap& tv, const CUtensorMap& tdo, const CUtensorMap& tdk,
+                                 const CUtensorMap& tdv, const CUtensorMap& tdqacc, const BwdArgs& a, float* dq_acc,
+                                 cudaStream_t s);
 // Box height of the backward's output store maps (one warp's 32 TMEM lanes).
 constexpr int kBwdStoreRows = 32;
 
@@ -66,6 +76,7 @@ cudaError_t launch_bwd_dq_f32(int D, bool causal, const BwdArgs& a, cudaStream_t
 cudaError_t launch_bwd_dkdv_f32(int D, bool causal, const BwdArgs& a, cudaStream_t s);
 
 // delta = rowsum(dO * O) in fp32 (fp16 or fp32 inputs).
+// delta = rowsum(dO * O); also zeroes the rows of a.dq_acc when it is set.
 cudaError_t launch_bwd_preprocess(int D, bool is_f16, const BwdArgs& a, cudaStream_t s);
 
 }  // namespace tattn

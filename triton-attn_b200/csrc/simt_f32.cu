@@ -277,6 +277,7 @@ __global__ void __launch_bounds__(SIMT_THREADS) bwd_dkdv_f32_kernel(BwdArgs a, b
 
 // delta[bh, i] = sum_d O[i, d] * dO[i, d] in fp32 (reference: _bwd_preprocess, kernels.py:324-337).
 // L lanes cooperate on one row with 16-byte loads; rows need a unit D stride and 16-byte alignment.
+// With a.dq_acc set (fused backward) the row's fp32 dQ workspace is zeroed as well.
 template <typename T, int D>
 __global__ void __launch_bounds__(256) preprocess_kernel(BwdArgs a) {
   constexpr int VEC = 16 / sizeof(T);  // elements per 16-byte load
@@ -316,6 +317,11 @@ __global__ void __launch_bounds__(256) preprocess_kernel(BwdArgs a) {
 #pragma unroll
   for (int off = L / 2; off > 0; off /= 2) acc += __shfl_xor_sync(0xffffffffu, acc, off);
   if (valid && sub == 0) a.delta[row_g] = acc;
+  if (valid && a.dq_acc != nullptr) {  // the fused backward's fp32 dQ row: D floats, D / L per lane
+    uint4* dst = reinterpret_cast<uint4*>(a.dq_acc + row_g * D + sub * (D / L));
+#pragma unroll
+    for (int e = 0; e < D / L / 4; ++e) dst[e] = make_uint4(0u, 0u, 0u, 0u);
+  }
 }
 
 template <int D>

@@ -26,6 +26,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tattn_bwd_dkdv": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I64P, _I, _I, _I, _I, _I, _I, _F, _I, _P]),
     "tattn_bwd_dq": (_I, [_P, _P, _P, _P, _P, _P, _P, _I64P, _I, _I, _I, _I, _I, _I, _F, _I, _P]),
     "tattn_bwd_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64P, _I, _I, _I, _I, _I, _I, _F, _P]),
+    "tattn_bwd_fused": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64P, _I, _I, _I, _I, _I, _I, _F, _P]),
     "tattn_layout_ok": (_I, [_P, _I64P, _I, _I, _I, _I]),
     "tattn_selftest_exp2": (_I, [_P, _P, _P, _P, _I, _P]),
     "tattn_tile_configs": (_I, [_I]),
