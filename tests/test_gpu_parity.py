@@ -221,22 +221,23 @@ def test_large_logits_small_scale(amp: float, scale: float) -> None:
 
 
 
+@pytest.mark.parametrize("causal", [False, True])
 @pytest.mark.parametrize("d", [16, 32, 64])
-def test_fused_backward_matches_three_kernel_path(d: int) -> None:
-    """tattn_bwd_fused (the default for non-causal fp16 D <= 64) against the reference's split into
+def test_fused_backward_matches_three_kernel_path(d: int, causal: bool) -> None:
+    """tattn_bwd_fused (the default for fp16 D <= 64) against the reference's split into
     preprocess, dK/dV and dQ kernels on the same inputs, N ragged (not a multiple of 128): dK and dV
     within fp16 rounding (same arithmetic) and bitwise reproducible, dQ (fp32 sums whose order
     varies) within the fp16 bound."""
     shape = (2, 3, 333, d)
     q, k, v, do = (_rand(shape, torch.float16, s) for s in (60, 61, 62, 63))
     scale = d**-0.5
-    o, m = api._forward(q, k, v, False, scale)
+    o, m = api._forward(q, k, v, causal, scale)
     assert api.FUSED_BACKWARD
-    fused = api._backward(q, k, v, o, m, do, False, scale)
-    again = api._backward(q, k, v, o, m, do, False, scale)
+    fused = api._backward(q, k, v, o, m, do, causal, scale)
+    again = api._backward(q, k, v, o, m, do, causal, scale)
     api.FUSED_BACKWARD = False
     try:
-        split = api._backward(q, k, v, o, m, do, False, scale)
+        split = api._backward(q, k, v, o, m, do, causal, scale)
     finally:
         api.FUSED_BACKWARD = True
     assert torch.equal(fused[1], again[1]) and torch.equal(fused[2], again[2])
@@ -244,7 +245,7 @@ def test_fused_backward_matches_three_kernel_path(d: int) -> None:
         err = (got.float() - want.float()).abs().max().item()
         assert err <= 2e-3, (key, err)
     qn, kn, vn, don = (_np(t) for t in (q, k, v, do))
-    for got, w in zip(fused, naive_gradients(qn, kn, vn, don, False, scale), strict=True):
+    for got, w in zip(fused, naive_gradients(qn, kn, vn, don, causal, scale), strict=True):
         _close(got, w, torch.float16, "fused grad")
 
 

@@ -1633,7 +1633,8 @@ cudaError_t dkdv_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtens
 }
 
 // ------------------------------------------------------------------- fused backward, D <= 64
-// dK, dV and dQ in one pass over each (key tile, query block) pair, so S^T, dP^T and the exponentials
+// dK, dV and dQ in one pass (non-causal, or causal with each key tile's query blocks starting at the
+// diagonal block; causal tiles are taken longest first) over each (key tile, query block) pair, so S^T, dP^T and the exponentials
 // are computed once instead of once per output kernel (the reference's split, kernels.py:151-321,
 // recomputes QK^T and dO V^T for dQ). The persistent dK/dV structure (one CTA per SM, 128-key tiles,
 // static round-robin, ring of Q/dO blocks; K double-buffered because the dQ MMAs read it to the end of
@@ -1707,7 +1708,7 @@ __device__ __forceinline__ void fused_dq_out(const uint32_t* o, uint32_t stg, co
   }
 }
 
-template <int D>
+template <int D, bool CAUSAL>
 __global__ void __launch_bounds__(kThreads, 1)
     bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
@@ -1746,7 +1747,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int zh = args.Z * args.H;
   const int nct = (N + 127) / 128;
   const int ntiles = nct * zh;
-  const int n = (N + BQ - 1) / BQ;  // query blocks of every tile (non-causal)
+  const int NBq = (N + BQ - 1) / BQ;
+  // Query blocks of key tile kt: [lo, NBq) (causal: from the diagonal block on).
+  auto tile_lo = [&](int kt) { return CAUSAL ? (128 * kt) / BQ : 0; };
+  // The CTA's it-th tile. Causal tiles come longest first and shrink steadily, so the assignment snakes
+  // (round r runs CTAs 0..G-1 forwards for even r, backwards for odd r) to pair long with short ones;
+  // a plain round-robin leaves the CTAs that start on the longest tiles ~14% behind at N = 16384.
+  auto cta_tile = [&](int it) {
+    const int G = int(gridDim.x), b = int(blockIdx.x);
+    return CAUSAL && (it & 1) ? it * G + (G - 1 - b) : it * G + b;
+  };
 
   if (threadIdx.x == 0) {
     for (int b = 0; b < 2; ++b) {
@@ -1795,10 +1805,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       // -------------------------------------------------------------- TMA producer + -M/-delta staging
       int g = 0, it = 0, kv_issued = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
+      for (int tile = cta_tile(0); ok && tile < ntiles; ++it, tile = cta_tile(it)) {
         int bh, kt;
-        dkdv_tile(tile, nct, zh, false, &bh, &kt);
-        const int zi = bh / args.H, hi = bh % args.H, k0 = 128 * kt;
+        dkdv_tile(tile, nct, zh, CAUSAL, &bh, &kt);
+        const int zi = bh / args.H, hi = bh % args.H, k0 = 128 * kt, lo = tile_lo(kt), n = NBq - lo;
         const int kb = it & 1;
         if (it >= 2 && !warp_wait(&bar_kv_empty[kb], ((it >> 1) - 1) & 1, ab)) { ok = false; break; }
         if (lane == 0) {
@@ -1812,7 +1822,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < n; ++c, ++g) {
           const int st = g % NS;
           if (g >= NS && !warp_wait(&bar_q_empty[st], ((g / NS) - 1) & 1, ab)) { ok = false; break; }
-          const int qr = c * BQ;
+          const int qr = (lo + c) * BQ;
           if (lane == 0) {
             mbar_arrive_expect_tx(&bar_q_full[st], 2 * C::T_Q);
             for (int ch = 0; ch < G::NCH; ++ch) {
@@ -1844,7 +1854,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t dDO = smem_desc(sDO, 16, 8 * G::SWB, G::LAYOUT);
       int g = 0, it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
+      for (int tile = cta_tile(0); ok && tile < ntiles; ++it, tile = cta_tile(it)) {
+        int bh, kt;
+        dkdv_tile(tile, nct, zh, CAUSAL, &bh, &kt);
+        const int n = NBq - tile_lo(kt);
         const int kb = it & 1;
         if (!warp_wait(&bar_kv_full[kb], (it >> 1) & 1, ab) || !warp_wait(bar_v_full, it & 1, ab)) {
           ok = false;
@@ -1875,7 +1888,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t dDSmn = smem_desc(sDS, C::DS_CHUNK, 1024, 2u);      // dS as MN-major A (dQ)
       int g = 0, it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
+      for (int tile = cta_tile(0); ok && tile < ntiles; ++it, tile = cta_tile(it)) {
+        int bh, kt;
+        dkdv_tile(tile, nct, zh, CAUSAL, &bh, &kt);
+        const int n = NBq - tile_lo(kt);
         const int kb = it & 1;
         const uint64_t ko = uint64_t((kb * C::T_KEY) >> 4);
         // The accumulators are overwritten by this tile's first MMAs: the previous tile's epilogue
@@ -1919,9 +1935,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // -------------------------------------------------------------- value tiles (warp 11)
       int it = 0, v_issued = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
+      for (int tile = cta_tile(0); ok && tile < ntiles; ++it, tile = cta_tile(it)) {
         int bh, kt;
-        dkdv_tile(tile, nct, zh, false, &bh, &kt);
+        dkdv_tile(tile, nct, zh, CAUSAL, &bh, &kt);
         if (it >= 1 && !warp_wait(bar_v_empty, (it - 1) & 1, ab)) { ok = false; break; }
         if (lane == 0) {
           mbar_arrive_expect_tx(bar_v_full, C::T_KEY);
@@ -1947,10 +1963,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float mul = w ? args.sm_scale : 1.f;
     int g = 0, it = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
+    for (int tile = cta_tile(0); ok && tile < ntiles; ++it, tile = cta_tile(it)) {
       int bh, kt;
-      dkdv_tile(tile, nct, zh, false, &bh, &kt);
-      const int zi = bh / args.H, hi = bh % args.H, k0 = 128 * kt;
+      dkdv_tile(tile, nct, zh, CAUSAL, &bh, &kt);
+      const int zi = bh / args.H, hi = bh % args.H, k0 = 128 * kt, lo = tile_lo(kt), n = NBq - lo;
       const int key = k0 + r;
       for (int c = 0; c < n; ++c, ++g) {
         const int st = g % NS;
@@ -1966,14 +1982,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(bar_s_free);  // the tensor core may now write S^T/dP^T of the next block
         if (!warp_wait(&bar_md_full[st], (g / NS) & 1, ab)) { ok = false; break; }
         const float* mq = md + st * 2 * BQ + w * H;
-        const int q0 = c * BQ + w * H;  // first query column of this warpgroup's half
-        const bool masked = (q0 + H > N) || (k0 + 128 > N);
-        const int c_hi = key < N ? N - q0 : 0;  // valid query columns: c < c_hi
+        const int q0 = (lo + c) * BQ + w * H;  // first query column of this warpgroup's half
+        const bool masked = (q0 + H > N) || (k0 + 128 > N) || (CAUSAL && q0 < k0 + 127);
+        const int c_lo = CAUSAL ? max(0, key - q0) : 0;  // valid query columns: c_lo <= c < c_hi
+        const int c_hi = key < N ? N - q0 : 0;
         uint32_t pt[H / 2], dst[H / 2];
         if (masked)
-          pds_row<H, true>(s, dp, mq, mq + BQ, pt, dst, scale2, 0, c_hi);
+          pds_row<H, true>(s, dp, mq, mq + BQ, pt, dst, scale2, c_lo, c_hi);
         else
-          pds_row<H, false>(s, dp, mq, mq + BQ, pt, dst, scale2, 0, c_hi);
+          pds_row<H, false>(s, dp, mq, mq + BQ, pt, dst, scale2, c_lo, c_hi);
         if (g > 0) {  // the previous block's dV/dK/dQ MMAs have read P^T and dS^T and written dQ_part
           if (!warp_wait(bar_acc_free, (g - 1) & 1, ab)) { ok = false; break; }
           tc_fence_after();
@@ -1998,7 +2015,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           reg_fence<C::HW>(oq);
           tc_fence_before();
           mbar_arrive(bar_dq_read);
-          fused_dq_out<D>(oq, stg, &tm_dqacc, w * C::HW, (c - 1) * BQ + 32 * q4, hi, zi, lane);
+          fused_dq_out<D>(oq, stg, &tm_dqacc, w * C::HW, (lo + c - 1) * BQ + 32 * q4, hi, zi, lane);
         } else {
           mbar_arrive(bar_dq_read);
         }
@@ -2015,7 +2032,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       reg_fence<C::HW>(oq);
       tc_fence_before();
       mbar_arrive(bar_acc_read);  // the next tile's first MMAs may overwrite the accumulators
-      fused_dq_out<D>(oq, stg, &tm_dqacc, w * C::HW, (n - 1) * BQ + 32 * q4, hi, zi, lane);
+      fused_dq_out<D>(oq, stg, &tm_dqacc, w * C::HW, (lo + n - 1) * BQ + 32 * q4, hi, zi, lane);
 #pragma unroll
       for (int half = 0; half < 2; ++half) {  // columns [half * HW, half * HW + HW)
         if (lane == 0) tma_store_wait_read_all();  // this warp's previous store has left the staging area
@@ -2061,11 +2078,11 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(const float4* __restric
   }
 }
 
-template <int D>
+template <int D, bool CAUSAL>
 cudaError_t fused_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tdo,
                        const CUtensorMap& tdk, const CUtensorMap& tdv, const CUtensorMap& tdqacc, const BwdArgs& a,
                        float* dq_acc, cudaStream_t s) {
-  auto kern = bwd_fused_kernel<D>;
+  auto kern = bwd_fused_kernel<D, CAUSAL>;
   constexpr int smem = FusedCfg<D>::SMEM_BYTES;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
@@ -2128,11 +2145,13 @@ cudaError_t launch_bwd_fused_f16(int D, bool causal, const CUtensorMap& tq, cons
                                  const CUtensorMap& tv, const CUtensorMap& tdo, const CUtensorMap& tdk,
                                  const CUtensorMap& tdv, const CUtensorMap& tdqacc, const BwdArgs& a, float* dq_acc,
                                  cudaStream_t s) {
-  if (causal) return cudaErrorNotSupported;
   switch (D) {
-    case 16: return fused_impl<16>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s);
-    case 32: return fused_impl<32>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s);
-    case 64: return fused_impl<64>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s);
+    case 16: return causal ? fused_impl<16, true>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s)
+                           : fused_impl<16, false>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s);
+    case 32: return causal ? fused_impl<32, true>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s)
+                           : fused_impl<32, false>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s);
+    case 64: return causal ? fused_impl<64, true>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s)
+                           : fused_impl<64, false>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s);
     default: return cudaErrorNotSupported;
   }
 }

@@ -301,7 +301,7 @@ extern "C" int tattn_bwd_fused(const void* q, const void* k, const void* v, cons
                                float sm_scale, void* stream) {
   if (!strides || !valid_dims(Z, H, N, D) || (dtype != TATTN_F16 && dtype != TATTN_F32))
     return TATTN_ERR_INVALID_ARGUMENT;
-  if (dtype != TATTN_F16 || causal || D > 64) return TATTN_ERR_UNSUPPORTED;
+  if (dtype != TATTN_F16 || D > 64) return TATTN_ERR_UNSUPPORTED;
   if (int64_t(Z) * H * N == 0) return TATTN_OK;
   if (!q || !k || !v || !o || !dout || !dq || !dk || !dv || !m || !delta || !dq_acc) return TATTN_ERR_INVALID_ARGUMENT;
   DeviceState* st;

@@ -57,11 +57,11 @@ cudaError_t launch_bwd_dq_f16(int D, bool causal, int tile_cfg, const CUtensorMa
 cudaError_t launch_bwd_dkdv_f16(int D, bool causal, int tile_cfg, const CUtensorMap& tq, const CUtensorMap& tk,
                                 const CUtensorMap& tv, const CUtensorMap& tdo, const CUtensorMap& tdk,
                                 const CUtensorMap& tdv, const BwdArgs& a, cudaStream_t s);
-// Fused backward (dK, dV and dQ in one kernel; non-causal, D <= 64): tq/tdo with 128-row boxes, tk/tv
+// Fused backward (dK, dV and dQ in one kernel; D <= 64, causal or not): tq/tdo with 128-row boxes, tk/tv
 // 128-row boxes, tdk/tdv store maps as above, tdqacc a reduce map over the dense fp32 workspace dq_acc
 // [Z, H, N, D] (kBwdStoreRows-row boxes of D/2 columns), zeroed beforehand (launch_bwd_preprocess with
 // a.dq_acc set). Runs the kernel, then writes a.dq = sm_scale * dq_acc as fp16. cudaErrorNotSupported
-// for other shapes.
+// for D = 128.
 cudaError_t launch_bwd_fused_f16(int D, bool causal, const CUtensorMap& tq, const CUtensorMap& tk,
                                  const CUtensorMap& tv, const CUtensorMap& tdo, const CUtensorMap& tdk,
                                  const CUtensorMap& tdv, const CUtensorMap& tdqacc, const BwdArgs& a, float* dq_acc,
