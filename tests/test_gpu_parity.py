@@ -249,6 +249,52 @@ def test_fused_backward_matches_three_kernel_path(d: int, causal: bool) -> None:
         _close(got, w, torch.float16, "fused grad")
 
 
+def test_entry_points_on_a_thread_that_has_not_used_cuda() -> None:
+    """Each C-ABI entry point as the first CUDA work of a new thread (the situation of the autograd
+    engine's worker thread): no CUDA context is current there until the library makes the device's
+    primary context current, and the tensor-map encoder it calls before any launch needs one.
+    Buffers are made on this thread; the new threads only call the library with raw pointers."""
+    import threading
+
+    lib = _lib.load()
+    shape, d, scale = (1, 2, 200, 64), 64, 0.125
+    q, k, v, do = (_rand(shape, torch.float16, s) for s in (70, 71, 72, 73))
+    o_ref, m_ref = api._forward(q, k, v, True, scale)
+    dq_ref, dk_ref, dv_ref = api._backward(q, k, v, o_ref, m_ref, do, True, scale)
+    o, dq, dk, dv = (torch.empty_like(q) for _ in range(4))
+    m, delta = (torch.empty(shape[:3], device=q.device, dtype=torch.float32) for _ in range(2))
+    ws = torch.empty(shape, device=q.device, dtype=torch.float32)
+    stream = torch.cuda.current_stream().cuda_stream
+    torch.cuda.synchronize()
+    st = [t.stride() for t in (q, k, v, o, do)]
+    fwd_strides = _lib.strides_array(st[0], st[1], st[2], st[3])
+    bwd_strides = _lib.strides_array(*st)
+    rcs: dict[str, int] = {}
+
+    def fwd() -> None:
+        rcs["fwd"] = lib.tattn_fwd(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), m.data_ptr(), fwd_strides,
+            *shape, 0, 1, scale, 0, stream,
+        )  # fmt: skip
+
+    def bwd() -> None:
+        rcs["bwd"] = lib.tattn_bwd_fused(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), o_ref.data_ptr(), do.data_ptr(), dq.data_ptr(),
+            dk.data_ptr(), dv.data_ptr(), m_ref.data_ptr(), delta.data_ptr(), ws.data_ptr(), bwd_strides,
+            *shape, 0, 1, scale, stream,
+        )  # fmt: skip
+
+    for fn in (fwd, bwd):
+        t = threading.Thread(target=fn)
+        t.start()
+        t.join()
+    torch.cuda.synchronize()
+    assert rcs == {"fwd": 0, "bwd": 0}, rcs
+    assert torch.equal(o, o_ref) and torch.equal(m, m_ref)
+    assert torch.equal(dk, dk_ref) and torch.equal(dv, dv_ref)
+    assert (dq.float() - dq_ref.float()).abs().max().item() <= 2e-3
+
+
 # --------------------------------------------------------------------------------- full sizes
 def _torch_ref(q, k, v, do, causal, scale):
     """fp32 materialised attention + autograd on the GPU (the definition, reference.py:18-26)."""

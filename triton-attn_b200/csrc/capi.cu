@@ -30,9 +30,13 @@ std::mutex g_mu;
 DeviceState g_dev[kMaxDevices];
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
+// The caller's current device. Also makes its primary context current on this thread: a thread that
+// has not used CUDA yet (e.g. the autograd engine's worker) has none, and the driver's tensor-map
+// encoder, called before any launch, then fails.
 int current_device(int* dev) {
   if (cudaGetDevice(dev) != cudaSuccess) return TATTN_ERR_CUDA;
   if (*dev < 0 || *dev >= kMaxDevices) return TATTN_ERR_NO_DEVICE;
+  if (cudaSetDevice(*dev) != cudaSuccess) return TATTN_ERR_CUDA;
   return TATTN_OK;
 }
 
