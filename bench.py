@@ -90,7 +90,10 @@ def peaks() -> dict:
 
 # ------------------------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clock / throttle samples every 50 ms while the timed region runs."""
+    """nvidia-smi clock / throttle samples every 50 ms while the timed region runs. Entering waits
+    (at most 5 s, before the region starts) for the first sample, since nvidia-smi takes longer to
+    start than a short timed region lasts; leaving waits (at most 0.3 s) for one more sample if none
+    arrived during the region. Only samples from the region's start on are summarised."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -100,6 +103,7 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc: subprocess.Popen | None = None
         self.lines: list[str] = []
+        self.first = 0
         self._t: threading.Thread | None = None
 
     def __enter__(self) -> ClockSampler:
@@ -111,6 +115,10 @@ class ClockSampler:
             )  # fmt: skip
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
+            t0 = time.monotonic()
+            while not self.lines and self.proc.poll() is None and time.monotonic() - t0 < 5.0:
+                time.sleep(0.005)
+            self.first = len(self.lines)
         except OSError:
             self.proc = None
         return self
@@ -122,6 +130,9 @@ class ClockSampler:
 
     def __exit__(self, *exc) -> None:
         if self.proc is not None:
+            t0 = time.monotonic()
+            while len(self.lines) <= self.first and self.proc.poll() is None and time.monotonic() - t0 < 0.3:
+                time.sleep(0.002)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -133,7 +144,7 @@ class ClockSampler:
     def summary(self) -> dict:
         sm, mx, reasons, power = [], None, set(), []
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in self.lines:
+        for line in self.lines[self.first:]:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
