@@ -46,7 +46,7 @@ CONFIGS = {
     "cfg3": (1, 16, 16384, 64, True),
     "cfg5": (64, 16, 8192, 64, True),  # scaling config: (batch, head) pairs split over the ranks
 }
-T4_PUBLISHED = {"cfg2": 16.9, "cfg3": 15.9}  # reference fwd+bwd TFLOP/s on a T4
+T4_PUBLISHED = {"cfg2": 16.9, "cfg3": 15.9}  # the reference's published fwd+bwd TFLOP/s on a T4 (results/t4.json)
 L2_BYTES = 126 * 2**20
 # DRAM bytes (read + write) of one launch of the dominant kernel, from the committed ncu capture
 # profiles/bwd_dkdv_cfg2.md (dram__bytes_read.sum + dram__bytes_write.sum); None for other configs.
@@ -485,7 +485,7 @@ def run_gpu(args) -> None:
             "higher_is_better": True,
             "scaling": "strong" if args.config == "cfg5" else "weak",
             "vs_baseline": round(value / T4_PUBLISHED[args.config], 2) if args.config in T4_PUBLISHED else None,
-            "vs_baseline_ref": "reference fwd+bwd on a Tesla T4 (BASELINE.md, results/t4.json)",
+            "vs_baseline_ref": "the reference's published fwd+bwd on a Tesla T4 (its results/t4.json)",
             "dtype": "fp16",
             "data": "synthetic: q,k,v,dO ~ N(0,1) cast to fp16, seeded per rank",
             "config": {
