@@ -1,17 +1,24 @@
 """Benchmark: attention fwd and fwd+bwd TFLOP/s (fp16, head_dim 64) on 1..8 B200s.
 
-One step = one forward + backward of ``tattn.attention`` over one batch (BASELINE config 2 per GPU:
-fp16, B4 H16 N4096 D64, non-causal; ``--config cfg3`` / ``cfg5`` select the causal long-context and
-the scaling configs). Multi-GPU runs shard (batch, head) pairs across ranks with no collective on the
-hot path (weak scaling: every rank runs the config-2 batch); each rank times on the device with CUDA
-events, rank 0 reports the max over ranks. FLOPs follow the reference (bench/bench.py:31-35):
-4*B*H*N^2*D, halved when causal, x3.5 for fwd+bwd.
+The headline line is BASELINE config 5, the scaling config: fp16 causal forward + backward over a fixed
+B64 H16 N8192 D64 problem whose 1,024 (batch, head) pairs are split evenly over the ranks (strong
+scaling; 1,024 / 512 / 256 / 128 pairs per GPU at 1 / 2 / 4 / 8 GPUs). One step = one forward and one
+backward of ``tattn.attention`` over the rank's pairs. Pairs are independent in the forward and the
+backward (the reference's grid axis 1 is Z*H, kernels.py:96-98), so ranks exchange no data; each rank
+times on the device with CUDA events and rank 0 reports the max over ranks. FLOPs follow the
+reference (bench/bench.py:31-35): 4*B*H*N^2*D, halved when causal, x3.5 for fwd+bwd.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2|cfg3|cfg5] [--impl reference]
+Configs 2 (B4 H16 N4096 non-causal) and 3 (B1 H16 N16384 causal) run on every rank as well, whole
+(they are single-GPU configs), and are reported per GPU under "configs": the north_star's forward
+target (>= 60% of peak) is stated on config 2. ``--config cfg2|cfg3`` makes one of them the headline
+instead (weak scaling: every rank runs the whole config).
 
-``--impl reference`` times the reference's CPU path (the oracle restatement of
-src/tattn/reference.py's tiled_forward/tiled_backward) on the host cores, on a bounded sample of the
-same workload, and prints the same JSON line with "impl": "reference".
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg5|cfg2|cfg3] [--impl reference]
+
+``--impl reference`` times the reference's CPU path (the numpy restatement of src/tattn/reference.py's
+tiled_forward / tiled_backward in oracle/) on the host cores: each step runs complete (batch, head)
+pairs of the same config, one per worker process, every key and query block of them, and the line
+reports their FLOPs over the step's wall time.
 
 ``--compare`` (one GPU) prints one JSON line per implementation and config, in the spirit of the
 reference's bench/bench.py comparison table (bench.py:62-76, 128-171): this library, torch's
@@ -41,16 +48,21 @@ for _p in (ROOT, os.path.join(ROOT, "triton-attn_b200")):
 
 METRIC = "attention fwd and fwd+bwd TFLOP/s (fp16, hd64) at 1/2/4/8 B200 vs fp16 peak"
 CONFIGS = {
-    # name: (batch per GPU, heads, seq, head_dim, causal)
+    # name: (batch, heads, seq, head_dim, causal)
     "cfg2": (4, 16, 4096, 64, False),
     "cfg3": (1, 16, 16384, 64, True),
-    "cfg5": (64, 16, 8192, 64, True),  # scaling config: (batch, head) pairs split over the ranks
+    "cfg5": (64, 16, 8192, 64, True),
 }
-T4_PUBLISHED = {"cfg2": 16.9, "cfg3": 15.9}  # the reference's published fwd+bwd TFLOP/s on a T4 (results/t4.json)
+STRONG = {"cfg5"}  # configs whose fixed (batch, head) pairs are split over the ranks
+# The reference's published fwd+bwd TFLOP/s on a Tesla T4 for the config-2 and config-3 shapes
+# (its results/t4.json); it publishes nothing for config 5.
+T4_PUBLISHED = {"cfg2": 16.9, "cfg3": 15.9}
 L2_BYTES = 126 * 2**20
-# DRAM bytes (read + write) of one launch of the dominant kernel, from the committed ncu capture
-# profiles/bwd_dkdv_cfg2.md (dram__bytes_read.sum + dram__bytes_write.sum); None for other configs.
-NCU_TRAFFIC = {("cfg2", "dkdv"): 136_370_176 + 43_040_000, ("cfg2", "bwd_fused"): 203_631_872 + 92_393_472}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the fused backward kernel
+# per (batch, head) pair, from an ncu capture of the current build on a 64-pair slice of each config
+# (inputs 5 x 64 MiB > L2), divided by the captured pairs; the summaries under profiles/ give the
+# commands and the raw figures. Scaled by the pairs a launch processes, as traffic grows with them.
+NCU_TRAFFIC_PER_PAIR: dict[tuple[str, str], float] = {}
 
 
 def flops(b: int, h: int, n: int, d: int, causal: bool, mode: str) -> float:
@@ -64,6 +76,33 @@ def shard(pairs: int, rank: int, world: int) -> tuple[int, int]:
     """Contiguous (batch, head) pair range [lo, hi) of `rank`: pairs are independent in the forward
     and the backward, so ranks need no data exchange; sizes differ by at most one pair."""
     return pairs * rank // world, pairs * (rank + 1) // world
+
+
+def local_pairs(cfg: str, rank: int, world: int) -> int:
+    """(batch, head) pairs one rank runs: its shard of a strong-scaling config, else the whole config."""
+    b, h = CONFIGS[cfg][:2]
+    if cfg in STRONG:
+        lo, hi = shard(b * h, rank, world)
+        return hi - lo
+    return b * h
+
+
+def config_dict(cfg: str, world: int) -> dict:
+    """The `config` object of the JSON line (identical in both arms)."""
+    b, h, n, d, causal = CONFIGS[cfg]
+    strong = cfg in STRONG
+    pairs = b * h
+    return {
+        "workload": (f"{cfg}: fp16 fwd+bwd B{b} H{h} N{n} D{d} {'causal' if causal else 'non-causal'}"
+                     + (f", {pairs} (batch, head) pairs split over {world} GPU(s)" if strong
+                        else f" on each of {world} GPU(s)")),  # fmt: skip
+        "global_batch_heads": pairs if strong else pairs * world,
+        "seq_len": n,
+        "head_dim": d,
+        "causal": causal,
+        "parallelism": f"(batch, head) sharding over {world} GPU(s), no collective on the hot path",
+        "l2": f"inputs {4 * (pairs // (world if strong else 1)) * n * d * 2 / 2**20:.0f} MiB per GPU per step > 126 MB L2",
+    }
 
 
 def max_over_ranks(ms: float, device=None) -> float:
@@ -165,98 +204,77 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------------------- CPU
-def _cpu_worker(args: tuple) -> tuple:
-    """Time the oracle's tiled forward+backward on (b, h) pairs [lo, hi), once with `blocks` and once
-    with 2*`blocks` outer blocks: (fwd_1, bwd_1, fwd_2, bwd_2) seconds."""
+def _cpu_init() -> None:
+    """Pool initializer: one BLAS thread per worker process (the workers already fill the cores)."""
+    for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[var] = "1"
+
+
+def _cpu_task(args: tuple) -> tuple[int, float, float]:
+    """One worker's share of a CPU step: the reference's tiled forward and backward (oracle restatement,
+    16x16 blocks, fp16 inputs upcast to fp32) over `npairs` complete (batch, head) pairs of length n.
+    Returns (pid, forward seconds, backward seconds); input generation is not timed."""
     import numpy as np
 
     from oracle import tiled_backward, tiled_forward
 
-    (b_h, n, d, causal, lo, hi, blocks, seed) = args
-    rng = np.random.default_rng(seed + lo)
-    shape = (hi - lo, n, d)
-    q, k, v, do = (rng.standard_normal(shape).astype(np.float16) for _ in range(4))
-    out = []
-    for nb in (blocks, 2 * blocks):
-        t0 = time.perf_counter()
-        o, m = tiled_forward(q, k, v, causal, row_blocks=nb)
-        t1 = time.perf_counter()
-        tiled_backward(q, k, v, o, m, do, causal, col_blocks=nb)
-        t2 = time.perf_counter()
-        out += [t1 - t0, t2 - t1]
-    return tuple(out)
+    n, d, causal, npairs, seed = args
+    rng = np.random.default_rng(seed)
+    q, k, v, do = (rng.standard_normal((npairs, n, d)).astype(np.float16) for _ in range(4))
+    t0 = time.perf_counter()
+    o, m = tiled_forward(q, k, v, causal)
+    t1 = time.perf_counter()
+    tiled_backward(q, k, v, o, m, do, causal)
+    t2 = time.perf_counter()
+    return os.getpid(), t1 - t0, t2 - t1
 
 
-def _pair_fraction(nb: int, taken: int, causal: bool, reverse: bool) -> float:
-    """Fraction of the block-pair loop covered by the first `taken` outer blocks (16x16 blocks)."""
-    if not causal:
-        return taken / nb
-    # forward: query block i does i+1 key blocks; backward: key block j does nb-j query blocks.
-    w = [(nb - i) if reverse else (i + 1) for i in range(nb)]
-    return sum(w[:taken]) / sum(w)
+def cpu_pool(workers: int):
+    """Spawned worker processes (spawn, so a pool started after CUDA initialisation is safe)."""
+    return mp.get_context("spawn").Pool(max(1, workers), initializer=_cpu_init)
 
 
-def cpu_pool(cfg: str, workers: int):
-    """A pool of `workers` spawned processes for cpu_baseline (spawned, so it is safe after CUDA init)."""
-    b, h = CONFIGS[cfg][:2]
-    return mp.get_context("spawn").Pool(max(1, min(workers, b * h)))
+def cpu_step(cfg: str, pool, workers: int, pairs_per_worker: int = 1, seed: int = 0) -> dict:
+    """One CPU step: `workers` tasks of `pairs_per_worker` whole pairs each, run in parallel. The step's
+    time is the busiest worker process's compute time (a process that ran two tasks counts both)."""
+    _, _, n, d, causal = CONFIGS[cfg]
+    tasks = [(n, d, causal, pairs_per_worker, seed * 1000 + i) for i in range(workers)]
+    res = pool.map(_cpu_task, tasks, chunksize=1)
+    per_pid: dict[int, list[float]] = {}
+    for pid, tf, tb in res:
+        acc = per_pid.setdefault(pid, [0.0, 0.0])
+        acc[0] += tf
+        acc[1] += tb
+    busiest = max(per_pid.values(), key=sum)
+    pairs = workers * pairs_per_worker
+    secs = sum(busiest)
+    return {"seconds": secs, "fwd_s": busiest[0], "bwd_s": busiest[1], "pairs": pairs,
+            "tflops": flops(1, pairs, n, d, causal, "fwd+bwd") / secs / 1e12}  # fmt: skip
 
 
-def _extrapolate(t1: float, t2: float, f1: float, f2: float) -> float:
-    """Full-loop time from samples t1, t2 covering loop fractions f1 < f2 of the block-pair loop:
-    t = setup + W * f, so W = (t2 - t1) / (f2 - f1) and full = setup + W (setup >= 0)."""
-    w = max(t2 - t1, 0.0) / max(f2 - f1, 1e-9)
-    return max(t1 - w * f1, 0.0) + w
-
-
-def cpu_baseline(cfg: str, budget_s: float, workers: int, pool=None, blocks: int | None = None) -> dict:
-    """The reference's CPU path (oracle restatement of reference.py's 16x16-block tiled forward and
-    backward, fp16 inputs upcast to fp32) on a bounded sample of the workload, in `workers` spawned
-    processes that split the (batch, head) pairs. Each worker times the first `blocks` and the first
-    2*`blocks` outer blocks; the difference gives the per-block cost without the fixed setup (fp32
-    copies, delta, output buffers), and the full-workload time is setup + the whole block loop.
-    Returns TFLOP/s for the full workload."""
+def cpu_sample_text(cfg: str, workers: int, pairs_per_worker: int) -> str:
     b, h, n, d, causal = CONFIGS[cfg]
-    pairs = b * h
-    nb = (n + 15) // 16
-    workers = max(1, min(workers, pairs))
-    bounds = [(pairs * i // workers, pairs * (i + 1) // workers) for i in range(workers)]
-    own = pool is None
-    if own:
-        pool = cpu_pool(cfg, workers)
-    try:
-        if blocks is None:  # size the sample from a one-block probe so it takes about budget_s
-            probe = pool.map(_cpu_worker, [(pairs, n, d, causal, lo, hi, 1, 0) for lo, hi in bounds])
-            per_blk = max((r[2] + r[3]) / 2 for r in probe)  # upper bound: setup included
-            blocks = max(1, min(nb // 2, int(budget_s / (3 * per_blk))))
-        res = pool.map(_cpu_worker, [(pairs, n, d, causal, lo, hi, blocks, 0) for lo, hi in bounds])
-    finally:
-        if own:
-            pool.close()
-            pool.join()
-    take = blocks
-    ff = [_pair_fraction(nb, take, causal, False), _pair_fraction(nb, 2 * take, causal, False)]
-    fb = [_pair_fraction(nb, take, causal, True), _pair_fraction(nb, 2 * take, causal, True)]
-    t_fwd = max(_extrapolate(r[0], r[2], *ff) for r in res)
-    t_bwd = max(_extrapolate(r[1], r[3], *fb) for r in res)
-    total = flops(b, h, n, d, causal, "fwd+bwd")
-    return {
-        "value": total / (t_fwd + t_bwd) / 1e12,
-        "unit": "TFLOP/s",
-        "cores": workers,
-        "kind": "port",
-        "sample": (f"{cfg} all {pairs} (b,h) pairs, first {take} and first {2 * take} of {nb} 16-row "
-                   f"query blocks (fwd) and key blocks (bwd); full time = setup + per-block cost x "
-                   f"block-pair count"),  # fmt: skip
-        "blocks": take,
-        "fwd_s_extrapolated": t_fwd,
-        "bwd_s_extrapolated": t_bwd,
-    }
+    return (f"{workers * pairs_per_worker} of the {b * h} (batch, head) pairs of {cfg} per step, each a complete "
+            f"N={n} D={d} {'causal' if causal else 'non-causal'} forward + backward (every 16x16 block of the "
+            f"reference's tiled loops), {pairs_per_worker} pair(s) in each of {workers} worker processes; "
+            f"TFLOP/s = the pairs' FLOPs / the busiest worker's compute time")  # fmt: skip
+
+
+def cpu_baseline(cfg: str, workers: int) -> dict:
+    """The `cpu_baseline` object of the GPU arm's line: one CPU step (after one warm-up step) on a pool of
+    `workers` processes, i.e. `workers` complete pairs of the same config."""
+    with cpu_pool(workers) as pool:
+        cpu_step(cfg, pool, workers, 1, seed=99)
+        r = cpu_step(cfg, pool, workers, 1, seed=1)
+    return {"value": round(r["tflops"], 6), "unit": "TFLOP/s", "cores": workers, "kind": "port",
+            "sample": cpu_sample_text(cfg, workers, 1), "seconds": round(r["seconds"], 2)}  # fmt: skip
 
 
 # ------------------------------------------------------------------------------------------- GPU
-def _kernel_times(q, k, v, do, causal, scale, iters: int) -> dict:
-    """Average device time (CUDA events on the launching stream) of each library kernel."""
+def _isolated_kernel_times(q, k, v, do, causal, scale, iters: int) -> dict:
+    """Average device time (CUDA events on the launching stream, back-to-back launches) of each entry
+    point on the rank's inputs: the forward, the fused backward call the API takes, and the
+    reference-style split backward (preprocess, dK/dV, dQ) for comparison."""
     import torch
 
     from tattn import _lib, api
@@ -282,7 +300,7 @@ def _kernel_times(q, k, v, do, causal, scale, iters: int) -> dict:
         "dq": lambda: lib.tattn_bwd_dq(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), dq.data_ptr(),
                                        m.data_ptr(), delta.data_ptr(), st, z, h, n, d, 0, ci, scale, 0, stream),
     }  # fmt: skip
-    if d <= 64:  # the backward the API runs for these shapes: delta, fused kernel, dQ scaling
+    if d <= 64:
         ws = torch.empty((z, h, n, d), device=q.device, dtype=torch.float32)
         st5 = _lib.strides_array(q.stride(), k.stride(), v.stride(), o.stride(), do.stride())
         calls["bwd_fused"] = lambda: lib.tattn_bwd_fused(
@@ -303,6 +321,79 @@ def _kernel_times(q, k, v, do, causal, scale, iters: int) -> dict:
     return out
 
 
+class _Timer:
+    """Device time of `iters` calls of `fn`: barrier, synchronize, CUDA events on the current stream,
+    synchronize; the max over ranks."""
+
+    def __init__(self, world: int, dev) -> None:
+        self.world, self.dev = world, dev
+
+    def __call__(self, fn, iters: int) -> float:
+        import torch
+        import torch.distributed as dist
+
+        if self.world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1), self.dev)
+
+
+def _inputs(pairs: int, n: int, d: int, dev, seed: int):
+    import torch
+
+    g = torch.Generator(device=dev).manual_seed(seed)
+    shape = (1, pairs, n, d)
+    return [torch.randn(shape, generator=g, device=dev).to(torch.float16) for _ in range(4)]
+
+
+def _side_config(cfg: str, steps: int, warmup: int, timer: _Timer, dev, rank: int, pk: dict) -> dict:
+    """Whole config `cfg` on this rank (weak): fwd+bwd and fwd-only device times, per GPU, max over ranks."""
+    import torch
+
+    from tattn import attention
+
+    b, h, n, d, causal = CONFIGS[cfg]
+    q, k, v, do = _inputs(b * h, n, d, dev, 4321 + rank)
+    q, k, v, do = (t.view(b, h, n, d) for t in (q, k, v, do))
+    qg, kg, vg = (t.detach().requires_grad_() for t in (q, k, v))
+
+    def step():
+        out = attention(qg, kg, vg, causal=causal)
+        return torch.autograd.grad(out, (qg, kg, vg), do)
+
+    def fwd():
+        with torch.no_grad():
+            return attention(q, k, v, causal=causal)
+
+    for _ in range(warmup):
+        step()
+        fwd()
+    ms_fb = timer(step, steps) / steps
+    ms_f = timer(fwd, steps) / steps
+    fb = flops(b, h, n, d, causal, "fwd+bwd") / (ms_fb * 1e-3) / 1e12
+    f = flops(b, h, n, d, causal, "fwd") / (ms_f * 1e-3) / 1e12
+    out = {
+        "workload": f"fp16 B{b} H{h} N{n} D{d} {'causal' if causal else 'non-causal'}, whole config on each GPU",
+        "fwd_bwd_tflops_per_gpu": round(fb, 2),
+        "fwd_bwd_ms": round(ms_fb, 4),
+        "fwd_tflops_per_gpu": round(f, 2),
+        "fwd_ms": round(ms_f, 4),
+        "fwd_frac_of_peak": round(f / pk["tflops"], 4),
+        "fwd_bwd_frac_of_peak": round(fb / pk["tflops"], 4),
+    }
+    if cfg in T4_PUBLISHED:
+        out["fwd_bwd_vs_t4_published"] = round(fb / T4_PUBLISHED[cfg], 2)
+    del q, k, v, do, qg, kg, vg
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_gpu(args) -> None:
     import torch
     import torch.distributed as dist
@@ -319,21 +410,34 @@ def run_gpu(args) -> None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    b, h, n, d, causal = CONFIGS[args.config]
-    if args.config == "cfg5":  # strong scaling of the fixed 1024 (b, h) pairs
-        lo, hi = shard(b * h, rank, world)
-        b_local, h_local = 1, hi - lo
-    else:  # weak scaling: each rank runs the whole config on its own (batch, head) shard
-        b_local, h_local = b, h
+    timer = _Timer(world, dev)
+    pk = peaks()
+    cfg = args.config
+    _, _, n, d, causal = CONFIGS[cfg]
+    pairs = args.pairs or local_pairs(cfg, rank, world)
     scale = 1.0 / math.sqrt(d)
-    shape = (b_local, h_local, n, d)
-    g = torch.Generator(device=dev).manual_seed(1234 + rank)
-    q, k, v, do = (torch.randn(shape, generator=g, device=dev).to(torch.float16) for _ in range(4))
+    shape = (1, pairs, n, d)
+    q, k, v, do = _inputs(pairs, n, d, dev, 1234 + rank)
     qg, kg, vg = (t.detach().requires_grad_() for t in (q, k, v))
 
     def step():
         out = attention(qg, kg, vg, causal=causal)
         return torch.autograd.grad(out, (qg, kg, vg), do)
+
+    # In-step split of the device time: events around the forward call and the backward call of every
+    # timed step (recorded on the launching stream; the host enqueues far ahead of these ms-long
+    # kernels, so each interval is the device time of that call's kernels).
+    marks: list[tuple] = []
+
+    def step_marked():
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        e[0].record()
+        out = attention(qg, kg, vg, causal=causal)
+        e[1].record()
+        grads = torch.autograd.grad(out, (qg, kg, vg), do)
+        e[2].record()
+        marks.append(e)
+        return grads
 
     def fwd_only():
         with torch.no_grad():
@@ -345,25 +449,19 @@ def run_gpu(args) -> None:
     if _lib.device_status() != 0:
         raise RuntimeError("device status word set during warm-up")
 
-    def timed(fn, iters):
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(iters):
-            fn()
-        e1.record()
-        torch.cuda.synchronize()
-        return max_over_ranks(e0.elapsed_time(e1), dev)
-
     with ClockSampler(local) as clk:
-        ms_total = timed(step, args.steps)
+        ms_total = timer(step_marked, args.steps)
     ms_step = ms_total / args.steps
+    fwd_in_step = statistics.fmean(m[0].elapsed_time(m[1]) for m in marks)
+    bwd_in_step = statistics.fmean(m[1].elapsed_time(m[2]) for m in marks)
+    split = torch.tensor([fwd_in_step, bwd_in_step], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(split, op=dist.ReduceOp.MAX)
+    fwd_in_step, bwd_in_step = split.tolist()
     if args.lean:  # profiling runs: warm-up + timed steps only
         if rank == 0:
-            total = flops(b_local, h_local, n, d, causal, "fwd+bwd") * world
-            print(json.dumps({"lean": True, "config": args.config, "ms_per_step": ms_step,
+            total = flops(1, pairs, n, d, causal, "fwd+bwd") * world
+            print(json.dumps({"lean": True, "config": cfg, "pairs_per_gpu": pairs, "ms_per_step": ms_step,
                               "tflops": total / (ms_step * 1e-3) / 1e12}), flush=True)  # fmt: skip
         if world > 1:
             dist.barrier()
@@ -371,15 +469,16 @@ def run_gpu(args) -> None:
         return
     for _ in range(3):
         fwd_only()
-    ms_fwd = timed(fwd_only, args.steps) / args.steps
+    ms_fwd = timer(fwd_only, args.steps) / args.steps
 
-    # e2e: every step copies its inputs q, k, v, dO from pinned host memory to the device, runs the
-    # public API's forward and backward, and copies O, dq, dk, dv back to pinned host memory.
-    # Serial: all on one stream. Pipelined (the reported value): copies on their own streams with two
-    # device input sets, so step k's compute overlaps step k+1's host->device copy and step k-1's
-    # device->host copy (PCIe is full duplex), as an input pipeline feeding a training loop would.
+    # ---- e2e: every step copies its inputs q, k, v, dO from pinned host memory to the device, runs the
+    # public API's forward and backward, and copies O, dq, dk, dv back into pinned host memory.
+    # Serial: all on one stream. Pipelined: copies on their own streams with two device input sets, so
+    # step k's compute overlaps step k+1's host->device copy and step k-1's device->host copy (PCIe is
+    # full duplex). Each step's outputs stay referenced until the compute stream has waited for their
+    # device->host copy, so the caching allocator reuses their memory only in stream order.
     host_in = [t.cpu().pin_memory() for t in (q, k, v, do)]
-    host_out = [[torch.empty(shape, dtype=torch.float16).pin_memory() for _ in range(4)] for _ in range(2)]
+    host_out = [torch.empty(shape, dtype=torch.float16).pin_memory() for _ in range(4)]
     dev_in = [[torch.empty(shape, device=dev, dtype=torch.float16) for _ in range(4)] for _ in range(2)]
     s_h2d, s_d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
 
@@ -392,17 +491,19 @@ def run_gpu(args) -> None:
     def e2e_serial_step():
         for dst, src in zip(dev_in[0], host_in):
             dst.copy_(src, non_blocking=True)
-        for dst, src in zip(host_out[0], compute_from(dev_in[0])):
+        for dst, src in zip(host_out, compute_from(dev_in[0])):
             dst.copy_(src, non_blocking=True)
 
-    def e2e_pipelined(iters):
+    def e2e_pipelined(iters: int) -> None:
         main = torch.cuda.current_stream(dev)
         in_ready = [torch.cuda.Event() for _ in range(2)]
         in_free = [torch.cuda.Event() for _ in range(2)]
+        out_copied = [torch.cuda.Event() for _ in range(2)]
+        held: list = [None, None]
         start = torch.cuda.Event()
         start.record(main)
 
-        def h2d(kk):
+        def h2d(kk: int) -> None:
             slot = kk % 2
             s_h2d.wait_event(start)
             if kk >= 2:
@@ -410,7 +511,7 @@ def run_gpu(args) -> None:
             with torch.cuda.stream(s_h2d):
                 for dst, src in zip(dev_in[slot], host_in):
                     dst.copy_(src, non_blocking=True)
-                in_ready[slot].record(s_h2d)
+            in_ready[slot].record(s_h2d)
 
         h2d(0)
         for kk in range(iters):
@@ -418,62 +519,67 @@ def run_gpu(args) -> None:
             if kk + 1 < iters:
                 h2d(kk + 1)
             main.wait_event(in_ready[slot])
+            if held[slot] is not None:  # step kk - 2's outputs have been copied out: release them
+                main.wait_event(out_copied[slot])
+                held[slot] = None
             outs = compute_from(dev_in[slot])
             in_free[slot].record(main)
             done = torch.cuda.Event()
             done.record(main)
             s_d2h.wait_event(done)
             with torch.cuda.stream(s_d2h):
-                for dst, src in zip(host_out[slot], outs):
+                for dst, src in zip(host_out, outs):
                     dst.copy_(src, non_blocking=True)
-                    src.record_stream(s_d2h)
-        tail = torch.cuda.Event()
-        tail.record(s_d2h)
-        main.wait_event(tail)  # the timed region ends after the last device->host copy
+            out_copied[slot].record(s_d2h)
+            held[slot] = outs
+        # The copy-out stream is in order: the timed region ends after its last copy.
+        main.wait_event(out_copied[(iters - 1) % 2])
 
-    def timed_pipelined(iters):
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        e2e_pipelined(iters)
-        e1.record()
-        torch.cuda.synchronize()
-        return max_over_ranks(e0.elapsed_time(e1), dev)
-
-    n_e2e = max(3, args.steps // 2)
+    n_e2e = max(3, args.steps)
     for _ in range(2):
         e2e_serial_step()
     e2e_pipelined(3)
     torch.cuda.synchronize()
-    ms_e2e_serial = timed(e2e_serial_step, n_e2e) / n_e2e
-    ms_e2e = timed_pipelined(n_e2e) / n_e2e
+    ms_e2e_serial = timer(e2e_serial_step, n_e2e) / n_e2e
+    ms_e2e_pipe = timer(lambda: e2e_pipelined(n_e2e), 1) / n_e2e
+    del dev_in
+    torch.cuda.empty_cache()
     if _lib.device_status() != 0:
         raise RuntimeError("device status word set during the timed region")
 
-    kt = _kernel_times(q, k, v, do, causal, scale, max(5, args.steps))
+    kt = _isolated_kernel_times(q.view(shape), k.view(shape), v.view(shape), do.view(shape), causal, scale,
+                                max(5, args.steps))  # fmt: skip
     if world > 1:
         kt_t = torch.tensor([kt[k_] for k_ in sorted(kt)], device=dev, dtype=torch.float64)
         dist.all_reduce(kt_t, op=dist.ReduceOp.MAX)
         kt = dict(zip(sorted(kt), kt_t.tolist()))
+    del q, k, v, do, qg, kg, vg
+    torch.cuda.empty_cache()
 
-    per_rank_fb = flops(b_local, h_local, n, d, causal, "fwd+bwd")
-    per_rank_f = flops(b_local, h_local, n, d, causal, "fwd")
-    total_fb = per_rank_fb * world
-    total_f = per_rank_f * world
+    side = {}
+    if not args.no_side:
+        for other in ("cfg2", "cfg3"):
+            if other != cfg:
+                side[other] = _side_config(other, args.steps, args.warmup, timer, dev, rank, pk)
+
+    # Pairs all ranks processed per step: the whole strong-scaling config (its shards), else every rank's own.
+    all_pairs = CONFIGS[cfg][0] * CONFIGS[cfg][1] if (cfg in STRONG and not args.pairs) else pairs * world
+    total_fb = flops(1, all_pairs, n, d, causal, "fwd+bwd")
+    total_f = flops(1, all_pairs, n, d, causal, "fwd")
     value = total_fb / (ms_step * 1e-3) / 1e12
     fwd_tflops = total_f / (ms_fwd * 1e-3) / 1e12
-    pk = peaks()
-    # GEMM FLOPs each kernel actually performs per launch (2 flops per MAC; causal halves the pairs).
-    pair_flops = 2.0 * b_local * h_local * n * n * d * (0.5 if causal else 1.0)
-    # bwd_fused: 5 GEMMs (S, dP, dV, dK, dQ) per pair; its time includes the delta pass and the dQ scaling.
-    kflops = {"fwd": 2 * pair_flops, "dkdv": 4 * pair_flops, "dq": 3 * pair_flops, "bwd_fused": 5 * pair_flops}
-    step_kernels = ("fwd", "bwd_fused") if "bwd_fused" in kt else ("fwd", "dkdv", "dq")  # what a step runs
-    dom = max(step_kernels, key=lambda kk: kt[kk])
-    achieved = kflops[dom] / (kt[dom] * 1e-3) / 1e12
-    bytes_in = 4 * b_local * h_local * n * d * 2
+    # GEMM FLOPs per launch on this rank (2 flops per MAC; causal halves the pairs): the forward's 2
+    # GEMMs; the fused backward's 5 (S, dP, dV, dK, dQ), whose call also runs the delta pass and the dQ
+    # scaling; the split path's 4 + 3.
+    pair_flops = 2.0 * pairs * n * n * d * (0.5 if causal else 1.0)
+    kflops = {"fwd": 2 * pair_flops, "bwd_fused": 5 * pair_flops, "dkdv": 4 * pair_flops, "dq": 3 * pair_flops}
+    step_kernels = {"fwd": fwd_in_step, "bwd_fused": bwd_in_step}
+    dom = max(step_kernels, key=lambda kk: step_kernels[kk])
+    achieved = kflops[dom] / (step_kernels[dom] * 1e-3) / 1e12
+    bytes_in = 4 * pairs * n * d * 2
+    traffic = NCU_TRAFFIC_PER_PAIR.get((cfg, dom))
     if rank == 0:
+        e2e_best = min(ms_e2e_serial, ms_e2e_pipe)
         line = {
             "metric": METRIC,
             "value": round(value, 2),
@@ -483,62 +589,65 @@ def run_gpu(args) -> None:
             "warmup": args.warmup,
             "ms_per_step": round(ms_step, 4),
             "higher_is_better": True,
-            "scaling": "strong" if args.config == "cfg5" else "weak",
-            "vs_baseline": round(value / T4_PUBLISHED[args.config], 2) if args.config in T4_PUBLISHED else None,
-            "vs_baseline_ref": "the reference's published fwd+bwd on a Tesla T4 (its results/t4.json)",
+            "scaling": "strong" if cfg in STRONG else "weak",
+            "vs_baseline": round(value / T4_PUBLISHED[cfg], 2) if cfg in T4_PUBLISHED else None,
             "dtype": "fp16",
             "data": "synthetic: q,k,v,dO ~ N(0,1) cast to fp16, seeded per rank",
-            "config": {
-                "workload": f"{args.config}: fp16 fwd+bwd B{b_local} H{h_local} N{n} D{d} "
-                            f"{'causal' if causal else 'non-causal'} per GPU",
-                "global_batch_heads": b_local * h_local * world,
-                "seq_len": n,
-                "head_dim": d,
-                "causal": causal,
-                "parallelism": f"(batch, head) sharding over {world} GPU(s), no collective on the hot path",
-                "l2": f"working set {8 * bytes_in // 4 / 2**20:.0f} MiB per step > 126 MB L2 (inputs larger than L2)",
-            },  # fmt: skip
+            "config": config_dict(cfg, world),
             "fwd_tflops": round(fwd_tflops, 2),
             "fwd_ms": round(ms_fwd, 4),
             "fwd_frac_of_peak": round(fwd_tflops / world / pk["tflops"], 4),
             "fwd_bwd_frac_of_peak": round(value / world / pk["tflops"], 4),
             "peak_tflops_per_gpu": pk["tflops"],
             "peak_source": f"{pk['source']} (MEASURED_PEAKS.json bf16_tflops, burst; fp16 dense equals bf16)",
-            "kernel_ms": {k_: round(v_, 4) for k_, v_ in kt.items()},
+            "in_step_ms": {"fwd": round(fwd_in_step, 4), "bwd": round(bwd_in_step, 4)},
+            "kernel_ms_isolated": {k_: round(v_, 4) for k_, v_ in kt.items()},
             "roofline": {
-                "kernel": dom,
+                "kernel": "bwd_fused_kernel (tattn_bwd_fused call)" if dom == "bwd_fused" else "fwd_f16_kernel",
                 "bound": "tensor",
                 "achieved": round(achieved, 1),
                 "peak": pk["tflops"],
                 "unit": "TFLOP/s",
                 "frac": round(achieved / pk["tflops"], 4),
-                "traffic": NCU_TRAFFIC.get((args.config, dom)),
-                "traffic_source": (f"ncu capture (profiles/{'bwd_fused' if dom == 'bwd_fused' else 'bwd_dkdv'}_cfg2.md)"
-                                   if (args.config, dom) in NCU_TRAFFIC else None),
+                "frac_of_sustained": round(achieved / pk["tflops_sustained"], 4) if pk.get("tflops_sustained") else None,
+                "traffic": round(traffic * pairs) if traffic else None,
+                "algorithmic_bytes": (9 if dom == "bwd_fused" else 4) * pairs * n * d * 2 + 8 * pairs * n,
                 "flops_per_launch": kflops[dom],
+                "timing": "CUDA events around each call inside the timed steps, mean over steps, max over ranks",
             },
             "e2e": {
-                "value": round(total_fb / (ms_e2e * 1e-3) / 1e12, 2),
+                "value": round(total_fb / (e2e_best * 1e-3) / 1e12, 2),
                 "unit": "TFLOP/s",
-                "ms_per_step": round(ms_e2e, 3),
+                "ms_per_step": round(e2e_best, 3),
                 "h2d_bytes_per_step": bytes_in,
                 "d2h_bytes_per_step": bytes_in,
-                "path": "tattn.attention with pinned host q,k,v,dO copied in and O,dq,dk,dv copied out every "
-                        "step; copies on their own streams, double-buffered, overlapping the neighbouring "
-                        "steps' compute",
+                "path": ("tattn.attention + autograd on each rank's pairs, with q, k, v, dO copied in from pinned "
+                         "host memory and O, dq, dk, dv copied back to pinned host memory every step; the "
+                         "faster of the two schedules below"),
+                "pipelined": {"value": round(total_fb / (ms_e2e_pipe * 1e-3) / 1e12, 2),
+                              "ms_per_step": round(ms_e2e_pipe, 3),
+                              "path": "copies on their own streams, double-buffered, overlapping the neighbouring "
+                                      "steps' compute"},
                 "serial": {"value": round(total_fb / (ms_e2e_serial * 1e-3) / 1e12, 2),
                            "ms_per_step": round(ms_e2e_serial, 3),
-                           "path": "the same with copies and compute on one stream"},
-            },
-            "gpu_launches": 4 * args.steps,
+                           "path": "copies and compute on one stream"},
+                "iterations": n_e2e,
+            },  # fmt: skip
+            "configs": side,
+            "gpu_launches": args.steps * LAUNCHES_PER_STEP,
             "clocks": clk.summary(),
         }
         if world == 1 and not args.no_cpu:
-            line["cpu_baseline"] = cpu_baseline(args.config, args.cpu_budget, max(1, os.cpu_count() or 1))
+            line["cpu_baseline"] = cpu_baseline(cfg, max(1, os.cpu_count() or 1))
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+# Library kernels one fwd+bwd step launches: the forward; the delta pass, the fused backward kernel and
+# the dQ scaling.
+LAUNCHES_PER_STEP = 4
 
 
 def run_compare(args) -> None:
@@ -632,28 +741,27 @@ def run_compare(args) -> None:
 
 
 def run_reference(args) -> None:
-    """The reference's CPU implementation of the path (oracle port), rank 0 only."""
+    """The reference's CPU implementation of the path (oracle restatement), rank 0 only: W warm-up steps,
+    then K timed steps, each `workers` complete (batch, head) pairs of the config in parallel."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
+    cfg = args.config
     cores = max(1, os.cpu_count() or 1)
-    vals = []
-    # Each step is one bounded sample of the same size (blocks sized once, from the first warm-up
-    # step, so that all steps together cost about cpu_budget seconds).
-    per_step = args.cpu_budget / max(1, args.steps)
-    with cpu_pool(args.config, cores) as pool:
-        first = cpu_baseline(args.config, per_step, cores, pool)
-        for _ in range(args.warmup - 1):
-            cpu_baseline(args.config, per_step, cores, pool, blocks=first["blocks"])
+    steps = []
+    t_start = time.perf_counter()
+    with cpu_pool(cores) as pool:
+        for i in range(args.warmup):
+            cpu_step(cfg, pool, cores, 1, seed=10_000 + i)
         t0 = time.perf_counter()
-        for _ in range(args.steps):
-            vals.append(cpu_baseline(args.config, per_step, cores, pool, blocks=first["blocks"]))
+        for i in range(args.steps):
+            steps.append(cpu_step(cfg, pool, cores, 1, seed=i))
         wall = time.perf_counter() - t0
-    b, h, n, d, causal = CONFIGS[args.config]
-    value = statistics.median(v["value"] for v in vals)
-    cb = dict(vals[-1])
-    cb["value"] = round(value, 6)
+    _, _, n, d, causal = CONFIGS[cfg]
+    pairs = steps[0]["pairs"]
+    secs = sum(s["seconds"] for s in steps)
+    value = flops(1, pairs * len(steps), n, d, causal, "fwd+bwd") / secs / 1e12
     line = {
         "metric": METRIC,
         "value": round(value, 6),
@@ -662,30 +770,33 @@ def run_reference(args) -> None:
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": round(flops(b, h, n, d, causal, "fwd+bwd") / (value * 1e12) * 1e3, 1),
+        "ms_per_step": round(secs / len(steps) * 1e3, 1),
         "higher_is_better": True,
-        "scaling": "strong" if args.config == "cfg5" else "weak",
+        "scaling": "strong" if cfg in STRONG else "weak",
         "vs_baseline": None,
-        "dtype": "fp16 inputs, fp32 arithmetic (reference CPU path)",
+        "dtype": "fp32 (fp16 inputs upcast, as the reference's CPU path does)",
         "data": "synthetic: q,k,v,dO ~ N(0,1) cast to fp16",
-        "config": {"workload": f"{args.config}: fp16 fwd+bwd B{b} H{h} N{n} D{d} {'causal' if causal else 'non-causal'}",
-                   "seq_len": n, "head_dim": d, "causal": causal},  # fmt: skip
-        "cpu_baseline": cb,
+        "config": config_dict(cfg, world),
+        "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                         "sample": cpu_sample_text(cfg, cores, 1)},
         "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "wall_s": round(wall, 1),
-    }
+        "total_wall_s": round(time.perf_counter() - t_start, 1),
+    }  # fmt: skip
     print(json.dumps(line), flush=True)
 
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg2")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg5")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU work for the CPU baseline")
+    ap.add_argument("--pairs", type=int, default=0,
+                    help="override the (batch, head) pairs per GPU (profiling a slice of a config)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-side", action="store_true", help="skip the extra per-GPU configs 2 and 3")
     ap.add_argument("--lean", action="store_true", help="warm-up + timed steps only (for profiler runs)")
     ap.add_argument("--compare", action="store_true",
                     help="comparison table against torch SDPA backends and a naive softmax (one GPU)")

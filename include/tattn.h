@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define TATTN_ABI_VERSION 1
+#define TATTN_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define TATTN_API __attribute__((visibility("default")))
@@ -56,7 +56,7 @@ enum tattn_status {
 };
 
 /* Device status word bits (tattn_device_status). */
-#define TATTN_DEV_WAIT_TIMEOUT 1 /* an mbarrier wait exceeded its 1 s limit; the CTA unwound */
+#define TATTN_DEV_WAIT_TIMEOUT 1 /* an mbarrier wait exceeded the wait limit (tattn_set_wait_limit_ns); the CTA unwound */
 #define TATTN_DEV_ABORTED 2
 
 /* Forward: O = softmax(Q K^T * sm_scale) V and M, for one attention call.
@@ -130,6 +130,22 @@ TATTN_API int tattn_tile_configs(int kind);
  * for part of each softmax row (y_poly), the hardware ex2.approx (y_hw) and CUDA's exp2f (y_lib), so
  * a test can hold the polynomial to its error bound against CUDA's own outputs. Device pointers. */
 TATTN_API int tattn_selftest_exp2(const float* x, float* y_poly, float* y_hw, float* y_lib, int n, void* stream);
+
+/* Bound of every wait inside the tensor-core kernels (no reference counterpart; the Triton kernels have
+ * no such waits). A wait that has not completed after limit_ns nanoseconds makes its CTA give up: it
+ * sets TATTN_DEV_WAIT_TIMEOUT in the device status word, drains its own copies in flight, frees its
+ * TMEM and exits, so a fault elsewhere can never leave a kernel spinning. Applies to launches made after
+ * the call, process-wide; 0 restores the default of 1 s. A limit shorter than a kernel's normal waits
+ * makes it fail (status set, outputs incomplete); keep the default outside tests. */
+TATTN_API int tattn_set_wait_limit_ns(uint64_t limit_ns);
+TATTN_API uint64_t tattn_get_wait_limit_ns(void);
+
+/* Diagnostic (no reference counterpart): one small kernel that runs the tensor-core kernels' unwinding
+ * path on purpose. Its first bounded wait is on a barrier that nothing completes, so after the current
+ * wait limit it records TATTN_DEV_WAIT_TIMEOUT, its other warp gives up through the CTA's abort flag, it
+ * frees its TMEM and returns. The GPU and the context stay usable; read (and clear) the bit with
+ * tattn_device_status. */
+TATTN_API int tattn_selftest_wait(void* stream);
 
 /* Synchronise `stream`, then report the current device's status word (TATTN_DEV_* bits) in *out and
  * clear it when `clear` is nonzero. Returns TATTN_OK, or TATTN_ERR_CUDA if the sync failed. */

@@ -91,3 +91,16 @@ def test_layout_rules(lib: ctypes.CDLL) -> None:
     assert ok(256, _lib.strides_array((7 * 70 * 16, 20, 7 * 20, 1)), 3, 7, 70, 16) == 0  # n stride 20: not 8-aligned
     # Strides of extent-1 dims are ignored.
     assert ok(256, _lib.strides_array((3, 5, 64, 1)), 1, 1, 9, 64) == 1
+
+
+def test_wait_limit_is_host_state(lib: ctypes.CDLL) -> None:
+    """The bound of the kernels' waits is a host-side setting (no GPU needed to set or read it);
+    0 restores the 1 s default."""
+    before = lib.tattn_get_wait_limit_ns()
+    try:
+        assert lib.tattn_set_wait_limit_ns(2_500_000) == _lib.OK
+        assert lib.tattn_get_wait_limit_ns() == 2_500_000
+        assert lib.tattn_set_wait_limit_ns(0) == _lib.OK
+        assert lib.tattn_get_wait_limit_ns() == 1_000_000_000
+    finally:
+        lib.tattn_set_wait_limit_ns(before)

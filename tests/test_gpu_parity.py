@@ -311,12 +311,18 @@ def _torch_ref(q, k, v, do, causal, scale):
 
 @pytest.mark.parametrize(
     "shape,causal,heads",
-    [((4, 16, 4096, 64), False, [(0, 0), (2, 13)]), ((1, 16, 16384, 64), True, [(0, 5)])],
-    ids=["cfg2_b4h16n4096", "cfg3_b1h16n16384_causal"],
+    [
+        ((4, 16, 4096, 64), False, [(0, 0), (1, 7), (2, 13), (3, 15)]),
+        ((1, 16, 16384, 64), True, [(0, 0), (0, 5), (0, 15)]),
+        ((64, 16, 8192, 64), True, [(0, 0), (21, 3), (42, 9), (63, 15)]),
+    ],
+    ids=["cfg2_b4h16n4096", "cfg3_b1h16n16384_causal", "cfg5_b64h16n8192_causal"],
 )
 def test_full_size_against_fp32_definition(shape, causal, heads) -> None:
-    """BASELINE configs 2 and 3 at full size; (batch, head) pairs checked against the fp32 definition.
-    Plain max-abs bound 2e-3 for O and dq/dk/dv (values are all well below 1 at these lengths)."""
+    """BASELINE configs 2, 3 and 5 at full size (config 5 is the scaling config: 1,024 pairs, 1 GiB per
+    tensor); (batch, head) pairs from the first, middle and last parts of the batch checked against the
+    fp32 definition. Plain max-abs bound 2e-3 for O and dq/dk/dv (values are all well below 1 at these
+    lengths), 1e-3 for M."""
     b, h, n, d = shape
     g = torch.Generator(device="cuda").manual_seed(2024)
     q, k, v, do = (torch.randn(shape, generator=g, device="cuda").to(torch.float16) for _ in range(4))

@@ -6,7 +6,8 @@ The entry point keeps delta in a fixed library-owned device array (TATTN_BWD_NOA
 shared by every call on a GPU. These tests call it through the C ABI twice in a row, on different
 problems, and compare each result with the regular entry points' (tattn_bwd_preprocess +
 tattn_bwd_dkdv + tattn_bwd_dq with a caller-allocated delta), within the parity tolerances of the
-GPU test-suite; and check that problems beyond the limit are refused before anything runs.
+GPU test-suite, and with the numpy oracle's gradients of the definition; and check that problems beyond
+the limit are refused before anything runs.
 This file is named so pytest collects it last.
 """
 
@@ -14,9 +15,11 @@ from __future__ import annotations
 
 import math
 
+import numpy as np
 import pytest
 import torch
 
+from oracle import naive_gradients
 from tattn import _lib, api
 
 pytestmark = pytest.mark.gpu
@@ -50,9 +53,10 @@ def _noalloc(q, k, v, o, do, m, causal, scale):
 @pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device")
 @pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
 def test_noalloc_matches_regular_backward_twice(dtype: torch.dtype) -> None:
-    # Two different problems back to back: the second call must not see the first call's leftovers
-    # in the shared array (the larger problem runs first, so stale rows exist beyond the second's).
-    cases = [((2, 4, 700, 64), True, 1), ((3, 2, 129, 32), False, 2)]
+    # Problems back to back: a later call must not see an earlier call's leftovers in the shared array
+    # (the larger problem runs first, so stale rows exist beyond the later ones'). Sequence lengths are
+    # not multiples of the kernels' 128-row blocks; D = 128 takes the D = 128 kernels through the array.
+    cases = [((2, 4, 700, 64), True, 1), ((3, 2, 129, 32), False, 2), ((1, 3, 333, 128), True, 3)]
     for shape, causal, seed in cases:
         q, k, v, o, do, m, scale = _case(shape, dtype, causal, seed)
         want = api._backward(q, k, v, o, m, do, causal, scale)
@@ -60,6 +64,11 @@ def test_noalloc_matches_regular_backward_twice(dtype: torch.dtype) -> None:
         torch.cuda.synchronize()
         for g, w, name in zip(got, want, ("dq", "dk", "dv"), strict=True):
             torch.testing.assert_close(g, w, **TOL[dtype], msg=lambda s, n=name: f"{n}: {s}")
+        # The same gradients against the oracle's (numpy, fp32) gradients of the definition.
+        qn, kn, vn, dn = (np.ascontiguousarray(t.float().cpu().numpy()) for t in (q, k, v, do))
+        for g, w, name in zip(got, naive_gradients(qn, kn, vn, dn, causal, scale), ("dq", "dk", "dv"), strict=True):
+            torch.testing.assert_close(g.float().cpu(), torch.as_tensor(w), **TOL[dtype],
+                                       msg=lambda s, n=name: f"{n} vs oracle: {s}")  # fmt: skip
     assert _lib.device_status() == 0
 
 

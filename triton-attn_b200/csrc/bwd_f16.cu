@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bar_fin = bar_s_full + 5;               // [2]: one per issuer warp
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
-  const CtaAbort ab{abort_flag, args.status};
+  const CtaAbort ab{abort_flag, args.status, args.wait_limit_ns};
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int N = args.N;
@@ -454,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bar_fin = bar_s_full + 6;           // [3]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
-  const CtaAbort ab{abort_flag, args.status};
+  const CtaAbort ab{abort_flag, args.status, args.wait_limit_ns};
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int N = args.N;
@@ -756,7 +756,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bar_tok = bar_s_full + 16;         // [2]: warpgroup w may start its exponentials
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
-  const CtaAbort ab{abort_flag, args.status};
+  const CtaAbort ab{abort_flag, args.status, args.wait_limit_ns};
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int N = args.N;
@@ -1092,7 +1092,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* md = reinterpret_cast<float*>(smem + C::OFF_MD);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
-  const CtaAbort ab{abort_flag, args.status};
+  const CtaAbort ab{abort_flag, args.status, args.wait_limit_ns};
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int N = args.N;
@@ -1403,7 +1403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* md = reinterpret_cast<float*>(smem + C::OFF_MD);  // per ring slot: -M [BQ] | -delta [BQ]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
-  const CtaAbort ab{abort_flag, args.status};
+  const CtaAbort ab{abort_flag, args.status, args.wait_limit_ns};
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int N = args.N;
@@ -1740,7 +1740,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* md = reinterpret_cast<float*>(smem + C::OFF_MD);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
-  const CtaAbort ab{abort_flag, args.status};
+  const CtaAbort ab{abort_flag, args.status, args.wait_limit_ns};
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int N = args.N;

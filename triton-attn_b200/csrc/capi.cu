@@ -5,9 +5,11 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "../../include/tattn.h"
+#include "common.cuh"
 #include "kernels.h"
 
 namespace tattn {
@@ -28,6 +30,8 @@ struct DeviceState {
 
 std::mutex g_mu;
 DeviceState g_dev[kMaxDevices];
+// Bound of every mbarrier wait in the kernels launched from now on (tattn_set_wait_limit_ns).
+std::atomic<unsigned long long> g_wait_limit_ns{kDefaultWaitLimitNs};
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 // The caller's current device. Also makes its primary context current on this thread: a thread that
@@ -167,6 +171,7 @@ extern "C" int tattn_fwd(const void* q, const void* k, const void* v, void* o, f
   a.H = H;
   a.N = N;
   a.status = st->status;
+  a.wait_limit_ns = g_wait_limit_ns.load();
   if (dtype == TATTN_F32) {
     a.qk_scale = sm_scale * kLog2e;
     return cuda_rc(launch_fwd_f32(D, causal != 0, q, k, v, sq, sk, sv, a, sm_scale, s));
@@ -253,6 +258,7 @@ int bwd_common(bool dq_pass, const void* q, const void* k, const void* v, const 
   a.qk_scale = (sm_scale < 0.f ? -sm_scale : sm_scale) * kLog2e;
   a.negate_s = sm_scale < 0.f ? 1 : 0;
   a.status = st->status;
+  a.wait_limit_ns = g_wait_limit_ns.load();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == TATTN_F32)
     return cuda_rc(dq_pass ? launch_bwd_dq_f32(D, causal != 0, a, s) : launch_bwd_dkdv_f32(D, causal != 0, a, s));
@@ -335,6 +341,7 @@ extern "C" int tattn_bwd_fused(const void* q, const void* k, const void* v, cons
   a.qk_scale = (sm_scale < 0.f ? -sm_scale : sm_scale) * kLog2e;
   a.negate_s = sm_scale < 0.f ? 1 : 0;
   a.status = st->status;
+  a.wait_limit_ns = g_wait_limit_ns.load();
   if (!layout_ok(q, a.sq, Z, H, N, D) || !layout_ok(k, a.sk, Z, H, N, D) || !layout_ok(v, a.sv, Z, H, N, D) ||
       !layout_ok(o, a.so, Z, H, N, D) || !layout_ok(dout, a.sdo, Z, H, N, D))
     return TATTN_ERR_LAYOUT;
@@ -354,6 +361,65 @@ extern "C" int tattn_bwd_fused(const void* q, const void* k, const void* v, cons
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((rc = cuda_rc(launch_bwd_preprocess(D, true, a, s))) != TATTN_OK) return rc;  // delta, zeroed dq_acc
   return cuda_rc(launch_bwd_fused_f16(D, causal != 0, tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s));
+}
+
+namespace tattn {
+namespace {
+
+// One CTA of two warps that runs the attention kernels' unwinding protocol without their data
+// movement. Warp 0 waits on a barrier phase that nothing completes; warp 1 waits on a barrier that warp
+// 0 would arrive on once its own wait succeeded. Warp 0's bounded wait runs out after the launch's wait
+// limit: it records kStatusWaitTimeout in the status word and raises the CTA's abort flag; warp 1 sees
+// the flag inside its own bounded wait and gives up as well; the TMEM columns allocated at the start
+// (as every tensor-core kernel here does) are released, and the kernel returns.
+__global__ void __launch_bounds__(64) wait_selftest_kernel(int* status, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x / 32;
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 32);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_slot, 32);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const CtaAbort ab{&abort_flag, status, limit_ns};
+  if (warp == 0) {
+    if (warp_wait(&bars[0], 0, ab)) mbar_arrive(&bars[1]);  // bars[0] never receives an arrival
+  } else {
+    warp_wait(&bars[1], 0, ab);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_slot, 32);
+  }
+}
+
+}  // namespace
+}  // namespace tattn
+
+extern "C" int tattn_set_wait_limit_ns(uint64_t limit_ns) {
+  g_wait_limit_ns.store(limit_ns == 0 ? kDefaultWaitLimitNs : static_cast<unsigned long long>(limit_ns));
+  return TATTN_OK;
+}
+
+extern "C" uint64_t tattn_get_wait_limit_ns(void) { return g_wait_limit_ns.load(); }
+
+extern "C" int tattn_selftest_wait(void* stream) {
+  DeviceState* st;
+  int rc = device_setup(&st);
+  if (rc != TATTN_OK) return rc;
+  wait_selftest_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(st->status, g_wait_limit_ns.load());
+  return cudaGetLastError() == cudaSuccess ? TATTN_OK : TATTN_ERR_CUDA;
 }
 
 extern "C" int tattn_layout_ok(const void* ptr, const int64_t* strides, int Z, int H, int N, int D) {

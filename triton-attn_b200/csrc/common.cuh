@@ -1,8 +1,9 @@
 // Shared device helpers for the sm_100a attention kernels: mbarriers with bounded waits, TMA tile
 // loads, tcgen05 (TMEM allocation, MMA issue/commit, TMEM loads/stores) and UMMA descriptors.
 //
-// Every wait in these kernels is bounded: a wait that has not completed after kWaitLimitNs sets a
-// bit in the caller-supplied status word and returns false, and the kernel then unwinds (drains its
+// Every wait in these kernels is bounded: a wait that has not completed after the launch's wait limit
+// (FwdArgs/BwdArgs::wait_limit_ns, set process-wide with tattn_set_wait_limit_ns; 1 s by default) sets
+// a bit in the caller-supplied status word and returns false, and the kernel then unwinds (drains its
 // own copies in flight, frees TMEM, exits) instead of spinning forever.
 #pragma once
 
@@ -14,11 +15,11 @@ namespace tattn {
 
 // Status bits written by kernels into the device status word (see include/tattn.h).
 enum : int {
-  kStatusWaitTimeout = 1 << 0,  // an mbarrier wait exceeded kWaitLimitNs
+  kStatusWaitTimeout = 1 << 0,  // an mbarrier wait exceeded the launch's wait limit
   kStatusAborted = 1 << 1,      // a CTA unwound because a sibling role timed out
 };
 
-constexpr unsigned long long kWaitLimitNs = 1000ull * 1000ull * 1000ull;  // 1 s
+constexpr unsigned long long kDefaultWaitLimitNs = 1000ull * 1000ull * 1000ull;  // 1 s
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -64,12 +65,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 
 // Per-CTA unwinding state shared by all roles of a warp-specialised kernel.
 struct CtaAbort {
-  volatile int* flag;  // shared memory: nonzero once any role of this CTA gave up
-  int* status;         // global status word
+  volatile int* flag;           // shared memory: nonzero once any role of this CTA gave up
+  int* status;                  // global status word
+  unsigned long long limit_ns;  // how long one wait may take before the CTA gives up
 };
 
 // Wait until the phase with the given parity of `bar` has completed. Returns false (after setting
-// the status bits and the CTA abort flag) if the wait exceeds kWaitLimitNs or another role of the
+// the status bits and the CTA abort flag) if the wait exceeds ab.limit_ns or another role of the
 // CTA has already given up.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const CtaAbort& ab) {
   const uint32_t a = smem_u32(bar);
@@ -79,7 +81,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
     if (mbar_try_wait(a, parity)) return true;
     if ((it & 63u) == 0) {
       if (*ab.flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > ab.limit_ns) {
         *ab.flag = 1;
         atomicOr(ab.status, kStatusWaitTimeout);
         return false;

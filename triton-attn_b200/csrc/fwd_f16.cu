@@ -186,7 +186,7 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* bar_p_full = bar_s_full + 10;            // [2]: the tile's softmax has stored P(j)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
-  const CtaAbort ab{abort_flag, args.status};
+  const CtaAbort ab{abort_flag, args.status, args.wait_limit_ns};
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int N = args.N;

@@ -21,6 +21,7 @@ struct FwdArgs {
   float qk_scale;    // |sm_scale| * log2(e); the sign goes into the S MMA (negate A) for fp16
   int negate_s;      // 1 when sm_scale < 0 (fp16 path)
   int* status;       // device status word
+  unsigned long long wait_limit_ns;  // bound of every mbarrier wait (tattn_set_wait_limit_ns)
 };
 
 struct BwdArgs {
@@ -37,6 +38,7 @@ struct BwdArgs {
   float qk_scale;    // |sm_scale| * log2(e)
   int negate_s;
   int* status;
+  unsigned long long wait_limit_ns;  // bound of every mbarrier wait (tattn_set_wait_limit_ns)
 };
 
 // Rows per K/V block of the fp16 forward for head dim D: the TMA box height of its K and V tensor maps

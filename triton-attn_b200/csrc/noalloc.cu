@@ -36,7 +36,10 @@ int g_scratch_rc[kMaxDevices] = {};
 float* g_scratch_ptr[kMaxDevices] = {};
 
 // Device address of g_delta_scratch on the current device (resolved once per device). The host-side
-// name `g_delta_scratch` is only a stand-in for the symbol and must never be passed to a kernel.
+// name `g_delta_scratch` is only a stand-in for the symbol and must never be passed to a kernel. The
+// device is checked first: on a GPU that is not sm_100 the library's kernels cannot load, so the symbol
+// cannot be resolved either, and the answer is TATTN_ERR_NO_DEVICE (the runtime's error from the
+// failed lookup, if any, is cleared so it does not surface in an unrelated later launch check).
 int scratch_for_current_device(float** out) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess) return TATTN_ERR_CUDA;
@@ -44,10 +47,20 @@ int scratch_for_current_device(float** out) {
   std::lock_guard<std::mutex> lock(g_scratch_mu);
   if (!g_scratch_init[dev]) {
     g_scratch_init[dev] = true;
+    int major = 0;
     void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_delta_scratch);
-    g_scratch_rc[dev] = (e == cudaSuccess && p != nullptr) ? TATTN_OK : TATTN_ERR_CUDA;
-    g_scratch_ptr[dev] = static_cast<float*>(p);
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) {
+      (void)cudaGetLastError();
+      g_scratch_rc[dev] = TATTN_ERR_CUDA;
+    } else if (major != 10) {
+      g_scratch_rc[dev] = TATTN_ERR_NO_DEVICE;
+    } else if (cudaGetSymbolAddress(&p, g_delta_scratch) != cudaSuccess || p == nullptr) {
+      (void)cudaGetLastError();
+      g_scratch_rc[dev] = TATTN_ERR_CUDA;
+    } else {
+      g_scratch_rc[dev] = TATTN_OK;
+      g_scratch_ptr[dev] = static_cast<float*>(p);
+    }
   }
   *out = g_scratch_ptr[dev];
   return g_scratch_rc[dev];
@@ -58,10 +71,11 @@ int scratch_for_current_device(float** out) {
 extern "C" int tattn_bwd_noalloc(const void* q, const void* k, const void* v, const void* o, const void* dout,
                                  void* dq, void* dk, void* dv, const float* m, const int64_t* strides, int Z,
                                  int H, int N, int D, int dtype, int causal, float sm_scale, void* stream) {
-  if (!strides || Z < 0 || H < 0 || N < 0) return TATTN_ERR_INVALID_ARGUMENT;
-  const long long rows = (long long)Z * H * N;
-  if (rows > kMaxRows) return TATTN_ERR_TOO_LARGE;
-  if (rows == 0) return TATTN_OK;
+  if (!strides || Z < 0 || H < 0 || N < 0 || (D != 16 && D != 32 && D != 64 && D != 128))
+    return TATTN_ERR_INVALID_ARGUMENT;
+  if (Z == 0 || H == 0 || N == 0) return TATTN_OK;
+  // Z*H*N rows, bounded without forming a product that could overflow.
+  if ((long long)N > kMaxRows / Z / H) return TATTN_ERR_TOO_LARGE;
   float* delta = nullptr;
   int rc = scratch_for_current_device(&delta);
   if (rc != TATTN_OK) return rc;

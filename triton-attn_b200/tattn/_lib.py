@@ -17,9 +17,11 @@ TATTN_F16, TATTN_F32 = 0, 1
 OK, ERR_INVALID_ARGUMENT, ERR_LAYOUT, ERR_CUDA, ERR_NO_DEVICE, ERR_DEVICE_STATUS, ERR_UNSUPPORTED = range(7)
 ERR_TOO_LARGE = 7
 BWD_NOALLOC_MAX_ROWS = 4194304  # TATTN_BWD_NOALLOC_MAX_ROWS
+DEV_WAIT_TIMEOUT, DEV_ABORTED = 1, 2  # device status word bits (TATTN_DEV_*)
 
 # Every symbol include/tattn.h declares, with its ctypes signature.
 _P, _I, _F, _I64P = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.POINTER(ctypes.c_int64)
+_U64 = ctypes.c_uint64
 SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tattn_fwd": (_I, [_P, _P, _P, _P, _P, _I64P, _I, _I, _I, _I, _I, _I, _F, _I, _P]),
     "tattn_bwd_preprocess": (_I, [_P, _P, _P, _I64P, _I, _I, _I, _I, _I, _P]),
@@ -29,12 +31,15 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tattn_bwd_fused": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64P, _I, _I, _I, _I, _I, _I, _F, _P]),
     "tattn_layout_ok": (_I, [_P, _I64P, _I, _I, _I, _I]),
     "tattn_selftest_exp2": (_I, [_P, _P, _P, _P, _I, _P]),
+    "tattn_selftest_wait": (_I, [_P]),
+    "tattn_set_wait_limit_ns": (_I, [_U64]),
+    "tattn_get_wait_limit_ns": (_U64, []),
     "tattn_tile_configs": (_I, [_I]),
     "tattn_device_status": (_I, [_P, ctypes.POINTER(ctypes.c_int), _I]),
     "tattn_status_string": (ctypes.c_char_p, [_I]),
     "tattn_abi_version": (_I, []),
 }
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
