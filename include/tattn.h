@@ -62,7 +62,7 @@ enum tattn_status {
 /* Forward: O = softmax(Q K^T * sm_scale) V and M, for one attention call.
  * Replaces the launch of _fwd_kernel (src/tattn/kernels.py:57-148) made by _forward
  * (src/tattn/api.py:78-99). strides: 16 int64 = q, k, v, o each (z, h, n, d).
- * tile_cfg: 0 = the tuned default; other values select tile variants (tattn_tile_configs). */
+ * tile_cfg: 0 = the default tile for (D, causal, dtype); 1..n = an explicit variant (tattn_tile_configs). */
 TATTN_API int tattn_fwd(const void* q, const void* k, const void* v, void* o, float* m, const int64_t* strides, int Z,
               int H, int N, int D, int dtype, int causal, float sm_scale, int tile_cfg, void* stream);
 
@@ -122,9 +122,23 @@ TATTN_API int tattn_bwd_noalloc(const void* q, const void* k, const void* v, con
  * strides: 4 int64 (z, h, n, d). Mirrors the check every fp16 entry point applies. */
 TATTN_API int tattn_layout_ok(const void* ptr, const int64_t* strides, int Z, int H, int N, int D);
 
-/* Number of tile variants per kernel family (valid tile_cfg values are 0 .. n-1); kind: 0 = forward,
- * 1 = backward. Stands in for the reference's autotune spaces (kernels.py:21-41); 0 is the default. */
+/* Tile variants. They stand in for the reference's autotune spaces (src/tattn/kernels.py:21-41, keyed
+ * per (N bucket, D, causal) at api.py:59-62) and for its explicit-config bypass (_launch, api.py:69-75):
+ * a static list per kernel family (kind 0 = forward, tattn_fwd; kind 1 = the split backward,
+ * tattn_bwd_dkdv and tattn_bwd_dq) and a fixed default per (D, causal, dtype) measured on a B200.
+ * tile_cfg 0 runs that default; tile_cfg i in 1..tattn_tile_configs(kind) runs variant i whatever the
+ * shape, and an fp16 call whose variant does not fit its head dim returns TATTN_ERR_UNSUPPORTED. fp32
+ * calls run CUDA-core kernels with no tile choice: tile_cfg is validated and otherwise ignored. */
+/* Number of explicit variants of family `kind` (0 for an unknown kind). */
 TATTN_API int tattn_tile_configs(int kind);
+/* Shape of variant tile_cfg (1-based): query rows per CTA (block_m), rows of each inner block the CTA
+ * loops over (block_n: keys in the forward and dQ pass, queries in the dK/dV pass), ring stages. */
+TATTN_API int tattn_tile_config_info(int kind, int tile_cfg, int* block_m, int* block_n, int* stages);
+/* The variant (1-based) that tile_cfg 0 runs for (D, causal, dtype); 0 when the dtype has no tile choice
+ * (fp32); -1 for an invalid kind, head dim or dtype. */
+TATTN_API int tattn_tile_default(int kind, int D, int causal, int dtype);
+/* 1 if variant tile_cfg of family `kind` can run fp16 head dim D (tile_cfg 0 always can), else 0. */
+TATTN_API int tattn_tile_supported(int kind, int tile_cfg, int D);
 
 /* Diagnostic (no reference counterpart): evaluate, for n inputs x, the FMA-pipe exp2 the kernels use
  * for part of each softmax row (y_poly), the hardware ex2.approx (y_hw) and CUDA's exp2f (y_lib), so

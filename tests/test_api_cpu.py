@@ -50,9 +50,42 @@ def test_tile_config_hook() -> None:
     assert api._tile_cfg(None, "fwd") == 0
     for kind, table in api.TILE_CONFIGS.items():
         for i, cfg in enumerate(table):
-            assert api._tile_cfg(cfg, kind) == i
-            assert api._tile_cfg({"tile_cfg": i}, kind) == i
+            assert api._tile_cfg(cfg, kind) == i + 1
+            assert api._tile_cfg({"tile_cfg": i + 1}, kind) == i + 1
+            # the reference's config dicts carry num_warps too; it has no meaning here and is ignored
+            assert api._tile_cfg({**cfg, "num_warps": 4}, kind) == i + 1
     with pytest.raises(ValueError):
         api._tile_cfg({"BLOCK_M": 3, "BLOCK_N": 5}, "fwd")
     with pytest.raises(ValueError):
         api._tile_cfg({"tile_cfg": 99}, "bwd")
+
+
+def test_tile_table_matches_the_library() -> None:
+    """api.TILE_CONFIGS is the library's table (csrc/tiles.h), and each family has several variants;
+    the default for every fp16 (D, causal) is one of them and can run that head dim."""
+    import ctypes
+
+    from tattn import _lib
+
+    lib = _lib.load()
+    for kind, table in api.TILE_CONFIGS.items():
+        k = api._KIND[kind]
+        assert lib.tattn_tile_configs(k) == len(table) >= 2
+        for i, cfg in enumerate(table):
+            bm, bn, st = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+            assert lib.tattn_tile_config_info(k, i + 1, bm, bn, st) == _lib.OK
+            assert cfg == {"BLOCK_M": bm.value, "BLOCK_N": bn.value, "num_stages": st.value}
+        assert lib.tattn_tile_config_info(k, 0, bm, bn, st) == _lib.ERR_INVALID_ARGUMENT
+        assert lib.tattn_tile_config_info(k, len(table) + 1, bm, bn, st) == _lib.ERR_INVALID_ARGUMENT
+        for d in (16, 32, 64, 128):
+            for causal in (0, 1):
+                t = lib.tattn_tile_default(k, d, causal, _lib.TATTN_F16)
+                assert 1 <= t <= len(table)
+                assert lib.tattn_tile_supported(k, t, d) == 1
+                assert lib.tattn_tile_default(k, d, causal, _lib.TATTN_F32) == 0
+        # 128-row inner blocks do not fit TMEM at D = 128; 64-row ones fit every head dim
+        for i, cfg in enumerate(table):
+            assert lib.tattn_tile_supported(k, i + 1, 128) == (cfg["BLOCK_N"] == 64)
+            assert lib.tattn_tile_supported(k, i + 1, 64) == 1
+            assert api.tile_supported(cfg, kind, 128) == (cfg["BLOCK_N"] == 64)
+    assert lib.tattn_tile_default(0, 48, 0, _lib.TATTN_F16) == -1

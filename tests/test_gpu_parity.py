@@ -183,24 +183,38 @@ def test_double_backward_is_refused_not_wrong() -> None:
         torch.autograd.grad(dq.sum(), k)
 
 
-@pytest.mark.parametrize("kind", ["fwd", "bwd"])
-def test_every_tile_config(kind: str) -> None:
-    """Every tile variant, bypassing the default choice (the reference's tests/test_configs.py)."""
-    for idx, cfg in enumerate(api.TILE_CONFIGS[kind]):
+def _tile_cases():
+    return [(kind, i) for kind, table in api.TILE_CONFIGS.items() for i in range(len(table))]
+
+
+@pytest.mark.parametrize("kind,idx", _tile_cases(), ids=lambda v: str(v))
+def test_every_tile_config(kind: str, idx: int) -> None:
+    """Every explicit tile variant, bypassing the default choice (the reference's tests/test_configs.py),
+    at every head dim it fits (an explicit variant that does not fit is refused, not run)."""
+    cfg = api.TILE_CONFIGS[kind][idx]
+    for d in (32, 64, 128):
+        if not api.tile_supported(cfg, kind, d):
+            q = torch.zeros(1, 1, 8, d, dtype=torch.float16, device="cuda")
+            with pytest.raises(_lib.TattnError):
+                if kind == "fwd":
+                    api._forward(q, q, q, False, 0.1, config=cfg)
+                else:
+                    o, m = api._forward(q, q, q, False, 0.1)
+                    api._backward(q, q, q, o, m, q, False, 0.1, config=cfg)
+            continue
         for n in (1, 37, 70, 300):
             for causal in (False, True):
-                g = torch.Generator().manual_seed(n)
-                q, k, v, do = (torch.randn(1, 2, n, 32, generator=g).to(torch.float16).cuda() for _ in range(4))
-                scale = 32**-0.5
+                g = torch.Generator().manual_seed(n + d)
+                q, k, v, do = (torch.randn(1, 2, n, d, generator=g).to(torch.float16).cuda() for _ in range(4))
+                scale = d**-0.5
                 fcfg = cfg if kind == "fwd" else None
                 bcfg = cfg if kind == "bwd" else None
                 o, m = api._forward(q, k, v, causal, scale, config=fcfg)
                 qn, kn, vn, don = (_np(t) for t in (q, k, v, do))
-                _close(o, naive_attention(qn, kn, vn, causal), torch.float16, f"cfg{idx} O")
+                _close(o, naive_attention(qn, kn, vn, causal), torch.float16, f"{kind}{idx} d{d} O")
                 dq, dk, dv = api._backward(q, k, v, o, m, do, causal, scale, config=bcfg)
                 for got, w in zip((dq, dk, dv), naive_gradients(qn, kn, vn, don, causal), strict=True):
-                    _close(got, w, torch.float16, f"cfg{idx} grad")
-
+                    _close(got, w, torch.float16, f"{kind}{idx} d{d} grad")
 
 
 @pytest.mark.parametrize("amp,scale", [(30.0, 1e-3), (100.0, 1.2e-4), (100.0, -1.2e-4), (100.0, 5e-5)])

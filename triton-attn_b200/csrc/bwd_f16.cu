@@ -37,6 +37,7 @@
 // commits for it (S/dP and accumulation) have landed.
 #include "common.cuh"
 #include "kernels.h"
+#include "tiles.h"
 
 namespace tattn {
 namespace {
@@ -91,11 +92,10 @@ __device__ __forceinline__ void mma_tmem_mn(uint32_t d_tmem, uint32_t a_tmem, ui
                      kk > 0 ? 1u : accumulate);
 }
 
-__device__ __forceinline__ int cta_order(int nct, int zh, bool longest_first, int* bh) {
-  if (longest_first) {
-    *bh = blockIdx.x % zh;
-    return blockIdx.x / zh;
-  }
+// CTA position of a one-tile-per-CTA grid: head-major when every tile costs the same; causal grids run
+// longest first within groups of heads (causal_cta_rank; 0 = the longest tile of its head).
+__device__ __forceinline__ int cta_order(int nct, int zh, bool longest_first, int N, int D, int* bh) {
+  if (longest_first) return causal_cta_rank(nct, zh, N, D, bh);
   *bh = blockIdx.x / nct;
   return blockIdx.x % nct;
 }
@@ -219,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int zh = args.Z * args.H;
   const int nct = (N + 127) / 128;
   int bh;
-  int cta = cta_order(nct, zh, CAUSAL, &bh);
+  int cta = cta_order(nct, zh, CAUSAL, N, D, &bh);
   if (CAUSAL) cta = nct - 1 - cta;  // longest-first: the highest query tiles see the most keys
   const int zi = bh / args.H, hi = bh % args.H;
   const int NBk = (N + C::BK - 1) / C::BK;
@@ -763,7 +763,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int zh = args.Z * args.H;
   const int nct = (N + 127) / 128;
   int bh;
-  int cta = cta_order(nct, zh, CAUSAL, &bh);
+  int cta = cta_order(nct, zh, CAUSAL, N, D, &bh);
   if (CAUSAL) cta = nct - 1 - cta;  // longest-first: the highest query tiles see the most keys
   const int zi = bh / args.H, hi = bh % args.H;
   const int NBk = (N + C::BK - 1) / C::BK;
@@ -1347,13 +1347,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------------- dK/dV: split columns
-// One CTA per 128-row key tile; query blocks of BQ (128, or 64 at D = 128 for the TMEM budget) whose
-// columns the two compute warpgroups split (warpgroup w takes columns [w*H, w*H + H), H = BQ/2).
+// One CTA per 128-row key tile; query blocks of BQ rows (the tile variant's block_n: 128, which fits
+// TMEM only for D <= 64, or 64) whose columns the two compute warpgroups split (warpgroup w takes
+// columns [w*H, w*H + H), H = BQ/2).
 // TMEM: S^T [BQ] | dP^T [BQ] | P^T [BQ/2] | dS^T [BQ/2] | dV [D] | dK [D].
-template <int D>
+template <int D, int BQ_>
 struct DkvSplitCfg {
   using G = Geo<D>;
-  static constexpr int BQ = D <= 64 ? 128 : 64;  // query rows per block
+  static constexpr int BQ = BQ_;                 // query rows per block
   static constexpr int H = BQ / 2;               // query columns per compute warpgroup
   static constexpr int NS = 4;                   // Q/dO ring stages
   static constexpr int T_KEY = G::tile(128);
@@ -1377,14 +1378,14 @@ struct DkvSplitCfg {
   static constexpr uint32_t IDESC_ACC = idesc_f16_f32(128, D, true);
 };
 
-template <int D, bool CAUSAL>
+template <int D, bool CAUSAL, int BQ>
 __global__ void __launch_bounds__(kThreads, 1)
     bwd_dkdv_split_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                     const BwdArgs args) {
-  using C = DkvSplitCfg<D>;
+  using C = DkvSplitCfg<D, BQ>;
   using G = Geo<D>;
-  constexpr int H = C::H, BQ = C::BQ;
+  constexpr int H = C::H;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
   const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
@@ -1411,7 +1412,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nct = (N + 127) / 128;
   int bh;
   // Causal: low key tiles see the most query blocks, so they go first.
-  const int cta = cta_order(nct, zh, CAUSAL, &bh);
+  const int cta = cta_order(nct, zh, CAUSAL, N, D, &bh);
   const int zi = bh / args.H, hi = bh % args.H;
   const int NBq = (N + BQ - 1) / BQ;
   const int k0 = 128 * cta;                 // keys [k0, k0 + 128)
@@ -1574,11 +1575,13 @@ cudaError_t launch_common(Kern kern, int smem, long long grid, const CUtensorMap
 
 int sm_count();
 
-template <int D, bool CAUSAL>
+// dQ pass of the split backward, tile variant with BK-row key blocks: 128 (D <= 64; persistent when every
+// tile costs the same, i.e. not causal) or 64 (the ping-pong kernel with alternating blocks).
+template <int D, bool CAUSAL, int BK>
 cudaError_t dq_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tdo,
                     const CUtensorMap& tdq, const BwdArgs& a, cudaStream_t s) {
   const long long tiles = (long long)((a.N + 127) / 128) * a.Z * a.H;
-  if constexpr (D <= 64 && !CAUSAL) {  // persistent only when every tile costs the same (as dK/dV)
+  if constexpr (BK == 128 && D <= 64 && !CAUSAL) {  // persistent only when every tile costs the same (as dK/dV)
     auto kern = bwd_dq_persist_kernel<D, CAUSAL>;
     constexpr int smem = DqPersistCfg<D>::SMEM_BYTES;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -1588,12 +1591,14 @@ cudaError_t dq_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensor
     const unsigned grid = unsigned(tiles < sm_count() ? tiles : sm_count());
     kern<<<dim3(grid), dim3(kThreads), smem, s>>>(tq, tk, tv, tdo, tdq, a);
     return cudaGetLastError();
-  } else if constexpr (D <= 64) {
+  } else if constexpr (BK == 128 && D <= 64) {
     (void)tdq;
     return launch_common(bwd_dq_split_kernel<D, CAUSAL>, DqSplitCfg<D>::SMEM_BYTES, tiles, tq, tk, tv, tdo, a, s);
-  } else {
+  } else if constexpr (BK == 64) {
     (void)tdq;
     return launch_common(bwd_dq_alt_kernel<D, CAUSAL>, DqAltCfg<D>::SMEM_BYTES, tiles, tq, tk, tv, tdo, a, s);
+  } else {
+    return cudaErrorNotSupported;
   }
 }
 
@@ -1609,13 +1614,14 @@ int sm_count() {
   return cache[dev];
 }
 
-template <int D, bool CAUSAL>
+// dK/dV pass of the split backward, tile variant with BQ-row query blocks: 128 (D <= 64; persistent
+// with static round-robin when every tile costs the same -- causal tiles differ, and the hardware's
+// dynamic CTA scheduling balances them better) or 64.
+template <int D, bool CAUSAL, int BQ>
 cudaError_t dkdv_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tdo,
                       const CUtensorMap& tdk, const CUtensorMap& tdv, const BwdArgs& a, cudaStream_t s) {
   const long long tiles = (long long)((a.N + 127) / 128) * a.Z * a.H;
-  // Persistent (static round-robin) when every tile costs the same; causal tiles differ, and the
-  // hardware's dynamic CTA scheduling balances them better.
-  if constexpr (D <= 64 && !CAUSAL) {
+  if constexpr (BQ == 128 && D <= 64 && !CAUSAL) {
     auto kern = bwd_dkdv_persist_kernel<D, CAUSAL>;
     constexpr int smem = DkvPersistCfg<D>::SMEM_BYTES;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -1625,10 +1631,13 @@ cudaError_t dkdv_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtens
     const unsigned grid = unsigned(tiles < sm_count() ? tiles : sm_count());
     kern<<<dim3(grid), dim3(kThreads), smem, s>>>(tq, tk, tv, tdo, tdk, tdv, a);
     return cudaGetLastError();
-  } else {
+  } else if constexpr (BQ == 64 || D <= 64) {
     (void)tdk;
     (void)tdv;
-    return launch_common(bwd_dkdv_split_kernel<D, CAUSAL>, DkvSplitCfg<D>::SMEM_BYTES, tiles, tq, tk, tv, tdo, a, s);
+    return launch_common(bwd_dkdv_split_kernel<D, CAUSAL, BQ>, DkvSplitCfg<D, BQ>::SMEM_BYTES, tiles, tq, tk, tv,
+                         tdo, a, s);
+  } else {
+    return cudaErrorNotSupported;
   }
 }
 
@@ -1750,12 +1759,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int NBq = (N + BQ - 1) / BQ;
   // Query blocks of key tile kt: [lo, NBq) (causal: from the diagonal block on).
   auto tile_lo = [&](int kt) { return CAUSAL ? (128 * kt) / BQ : 0; };
-  // The CTA's it-th tile. Causal tiles come longest first and shrink steadily, so the assignment snakes
-  // (round r runs CTAs 0..G-1 forwards for even r, backwards for odd r) to pair long with short ones;
-  // a plain round-robin leaves the CTAs that start on the longest tiles ~14% behind at N = 16384.
-  auto cta_tile = [&](int it) {
-    const int G = int(gridDim.x), b = int(blockIdx.x);
-    return CAUSAL && (it & 1) ? it * G + (G - 1 - b) : it * G + b;
+  // The CTA's key tiles, in processing order (every role walks the same sequence). Not causal: the
+  // head-major tile list round-robin (CTA b: tiles b, b + G, ...). Causal: key tiles kt and nct-1-kt of a
+  // head together cost nct + 1 query blocks whatever kt is, so they form one unit of work (a middle tile
+  // of odd nct is a unit alone); units are taken round-robin in head-major order, the longer tile of a
+  // unit first. Equal units balance the CTAs, and the tiles running at any time belong to a few
+  // neighbouring heads, so their fp32 dQ workspace rows and Q/dO blocks are shared in L2 (ordering the
+  // tiles longest-first across all heads instead spreads 148 CTAs over ~148 heads, whose workspaces miss
+  // L2: ~10x the algorithmic DRAM traffic at N = 8192 with 1,024 heads).
+  const int n_units = CAUSAL ? zh * ((nct + 1) / 2) : ntiles;
+  auto next_tile = [&](int2& seq, int* bh, int* kt) -> bool {  // seq = (unit, second tile of the unit)
+    if (seq.x >= n_units) return false;
+    if (!CAUSAL) {
+      *bh = seq.x / nct;
+      *kt = seq.x % nct;
+      seq.x += int(gridDim.x);
+      return true;
+    }
+    const int U = (nct + 1) / 2, p = seq.x % U;
+    *bh = seq.x / U;
+    *kt = seq.y ? nct - 1 - p : p;
+    if (seq.y || nct - 1 - p == p) {
+      seq = make_int2(seq.x + int(gridDim.x), 0);
+    } else {
+      seq.y = 1;
+    }
+    return true;
   };
 
   if (threadIdx.x == 0) {
@@ -1805,9 +1834,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // -------------------------------------------------------------- TMA producer + -M/-delta staging
       int g = 0, it = 0, kv_issued = 0;
       bool ok = true;
-      for (int tile = cta_tile(0); ok && tile < ntiles; ++it, tile = cta_tile(it)) {
-        int bh, kt;
-        dkdv_tile(tile, nct, zh, CAUSAL, &bh, &kt);
+      int2 seq = make_int2(int(blockIdx.x), 0);
+      for (int bh, kt; ok && next_tile(seq, &bh, &kt); ++it) {
         const int zi = bh / args.H, hi = bh % args.H, k0 = 128 * kt, lo = tile_lo(kt), n = NBq - lo;
         const int kb = it & 1;
         if (it >= 2 && !warp_wait(&bar_kv_empty[kb], ((it >> 1) - 1) & 1, ab)) { ok = false; break; }
@@ -1854,9 +1882,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t dDO = smem_desc(sDO, 16, 8 * G::SWB, G::LAYOUT);
       int g = 0, it = 0;
       bool ok = true;
-      for (int tile = cta_tile(0); ok && tile < ntiles; ++it, tile = cta_tile(it)) {
-        int bh, kt;
-        dkdv_tile(tile, nct, zh, CAUSAL, &bh, &kt);
+      int2 seq = make_int2(int(blockIdx.x), 0);
+      for (int bh, kt; ok && next_tile(seq, &bh, &kt); ++it) {
         const int n = NBq - tile_lo(kt);
         const int kb = it & 1;
         if (!warp_wait(&bar_kv_full[kb], (it >> 1) & 1, ab) || !warp_wait(bar_v_full, it & 1, ab)) {
@@ -1888,9 +1915,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t dDSmn = smem_desc(sDS, C::DS_CHUNK, 1024, 2u);      // dS as MN-major A (dQ)
       int g = 0, it = 0;
       bool ok = true;
-      for (int tile = cta_tile(0); ok && tile < ntiles; ++it, tile = cta_tile(it)) {
-        int bh, kt;
-        dkdv_tile(tile, nct, zh, CAUSAL, &bh, &kt);
+      int2 seq = make_int2(int(blockIdx.x), 0);
+      for (int bh, kt; ok && next_tile(seq, &bh, &kt); ++it) {
         const int n = NBq - tile_lo(kt);
         const int kb = it & 1;
         const uint64_t ko = uint64_t((kb * C::T_KEY) >> 4);
@@ -1935,9 +1961,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // -------------------------------------------------------------- value tiles (warp 11)
       int it = 0, v_issued = 0;
       bool ok = true;
-      for (int tile = cta_tile(0); ok && tile < ntiles; ++it, tile = cta_tile(it)) {
-        int bh, kt;
-        dkdv_tile(tile, nct, zh, CAUSAL, &bh, &kt);
+      int2 seq = make_int2(int(blockIdx.x), 0);
+      for (int bh, kt; ok && next_tile(seq, &bh, &kt); ++it) {
         if (it >= 1 && !warp_wait(bar_v_empty, (it - 1) & 1, ab)) { ok = false; break; }
         if (lane == 0) {
           mbar_arrive_expect_tx(bar_v_full, C::T_KEY);
@@ -1963,9 +1988,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float mul = w ? args.sm_scale : 1.f;
     int g = 0, it = 0;
     bool ok = true;
-    for (int tile = cta_tile(0); ok && tile < ntiles; ++it, tile = cta_tile(it)) {
-      int bh, kt;
-      dkdv_tile(tile, nct, zh, CAUSAL, &bh, &kt);
+    int2 seq = make_int2(int(blockIdx.x), 0);
+    for (int bh, kt; ok && next_tile(seq, &bh, &kt); ++it) {
       const int zi = bh / args.H, hi = bh % args.H, k0 = 128 * kt, lo = tile_lo(kt), n = NBq - lo;
       const int key = k0 + r;
       for (int c = 0; c < n; ++c, ++g) {
@@ -2086,11 +2110,13 @@ cudaError_t fused_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUten
   constexpr int smem = FusedCfg<D>::SMEM_BYTES;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  const long long tiles = (long long)((a.N + 127) / 128) * a.Z * a.H;
+  const long long nct = (a.N + 127) / 128;
+  const long long tiles = nct * a.Z * a.H;
   if (tiles <= 0) return cudaSuccess;
   if (tiles > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
   const long long count = (long long)a.Z * a.H * a.N * D;
-  const unsigned grid = unsigned(tiles < sm_count() ? tiles : sm_count());
+  const long long units = CAUSAL ? (nct + 1) / 2 * a.Z * a.H : tiles;  // the kernel's next_tile units
+  const unsigned grid = unsigned(units < sm_count() ? units : sm_count());
   kern<<<dim3(grid), dim3(kThreads), smem, s>>>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   const long long n8 = count / 8;  // D is a multiple of 8
@@ -2102,43 +2128,64 @@ cudaError_t fused_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUten
 
 }  // namespace
 
-void bwd_f16_box_rows(int D, bool dq_pass, int* q_rows, int* kv_rows) {
-  // dQ: 128-row query tiles; key blocks of DqSplitCfg::BK rows (D <= 64) or DqAltCfg::BK rows (D = 128).
-  // dK/dV: 128-row key tiles; query blocks of DkvPersistCfg::BQ (D <= 64) or DkvSplitCfg::BQ rows.
-  const bool wide = D <= 64;
-  if (dq_pass) {
-    *q_rows = 128;
-    *kv_rows = wide ? DqSplitCfg<64>::BK : DqAltCfg<128>::BK;
-  } else {
-    *q_rows = wide ? DkvPersistCfg<64>::BQ : DkvSplitCfg<128>::BQ;
-    *kv_rows = 128;
-  }
+void bwd_f16_box_rows(int D, bool dq_pass, int variant, int* q_rows, int* kv_rows) {
+  // dQ: 128-row query tiles; key blocks of the variant's block_n rows (the kernels' BK).
+  // dK/dV: 128-row key tiles; query blocks of block_n rows (DkvPersistCfg::BQ or DkvSplitCfg::BQ).
+  static_assert(DqSplitCfg<64>::BK == 128 && DqPersistCfg<64>::BK == 128 && DqAltCfg<64>::BK == 64, "dQ blocks");
+  static_assert(DkvPersistCfg<64>::BQ == 128 && DkvSplitCfg<64, 64>::BQ == 64, "dK/dV blocks");
+  const int bn = tile_supported(1, variant, D) ? kBwdTiles[variant].block_n : 0;
+  *q_rows = dq_pass ? 128 : bn;
+  *kv_rows = dq_pass ? bn : 128;
 }
 
-cudaError_t launch_bwd_dq_f16(int D, bool causal, int tile_cfg, const CUtensorMap& tq, const CUtensorMap& tk,
+namespace {
+template <bool DQ, int D, bool CAUSAL>
+cudaError_t split_variant(int variant, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                          const CUtensorMap& tdo, const CUtensorMap& t0, const CUtensorMap& t1, const BwdArgs& a,
+                          cudaStream_t s) {
+  static_assert(kNumBwdTiles == 2 && kBwdTiles[0].block_n == 128 && kBwdTiles[1].block_n == 64, "variant dispatch");
+  if (variant == 0) {
+    if constexpr (D <= 64) {
+      if constexpr (DQ) return dq_impl<D, CAUSAL, 128>(tq, tk, tv, tdo, t0, a, s);
+      else return dkdv_impl<D, CAUSAL, 128>(tq, tk, tv, tdo, t0, t1, a, s);
+    }
+    return cudaErrorNotSupported;
+  }
+  if constexpr (DQ) return dq_impl<D, CAUSAL, 64>(tq, tk, tv, tdo, t0, a, s);
+  else return dkdv_impl<D, CAUSAL, 64>(tq, tk, tv, tdo, t0, t1, a, s);
+}
+
+template <bool DQ>
+cudaError_t split_dispatch(int D, bool causal, int variant, const CUtensorMap& tq, const CUtensorMap& tk,
+                           const CUtensorMap& tv, const CUtensorMap& tdo, const CUtensorMap& t0,
+                           const CUtensorMap& t1, const BwdArgs& a, cudaStream_t s) {
+  if (!tile_supported(1, variant, D)) return cudaErrorNotSupported;
+#define TATTN_SPLIT_CASE(DD)                                                                      \
+  case DD:                                                                                        \
+    return causal ? split_variant<DQ, DD, true>(variant, tq, tk, tv, tdo, t0, t1, a, s)           \
+                  : split_variant<DQ, DD, false>(variant, tq, tk, tv, tdo, t0, t1, a, s);
+  switch (D) {
+    TATTN_SPLIT_CASE(16)
+    TATTN_SPLIT_CASE(32)
+    TATTN_SPLIT_CASE(64)
+    TATTN_SPLIT_CASE(128)
+    default:
+      return cudaErrorInvalidValue;
+  }
+#undef TATTN_SPLIT_CASE
+}
+}  // namespace
+
+cudaError_t launch_bwd_dq_f16(int D, bool causal, int variant, const CUtensorMap& tq, const CUtensorMap& tk,
                               const CUtensorMap& tv, const CUtensorMap& tdo, const CUtensorMap& tdq, const BwdArgs& a,
                               cudaStream_t s) {
-  (void)tile_cfg;
-  switch (D) {
-    case 16: return causal ? dq_impl<16, true>(tq, tk, tv, tdo, tdq, a, s) : dq_impl<16, false>(tq, tk, tv, tdo, tdq, a, s);
-    case 32: return causal ? dq_impl<32, true>(tq, tk, tv, tdo, tdq, a, s) : dq_impl<32, false>(tq, tk, tv, tdo, tdq, a, s);
-    case 64: return causal ? dq_impl<64, true>(tq, tk, tv, tdo, tdq, a, s) : dq_impl<64, false>(tq, tk, tv, tdo, tdq, a, s);
-    case 128: return causal ? dq_impl<128, true>(tq, tk, tv, tdo, tdq, a, s) : dq_impl<128, false>(tq, tk, tv, tdo, tdq, a, s);
-    default: return cudaErrorInvalidValue;
-  }
+  return split_dispatch<true>(D, causal, variant, tq, tk, tv, tdo, tdq, tdq, a, s);
 }
 
-cudaError_t launch_bwd_dkdv_f16(int D, bool causal, int tile_cfg, const CUtensorMap& tq, const CUtensorMap& tk,
+cudaError_t launch_bwd_dkdv_f16(int D, bool causal, int variant, const CUtensorMap& tq, const CUtensorMap& tk,
                                 const CUtensorMap& tv, const CUtensorMap& tdo, const CUtensorMap& tdk,
                                 const CUtensorMap& tdv, const BwdArgs& a, cudaStream_t s) {
-  (void)tile_cfg;
-  switch (D) {
-    case 16: return causal ? dkdv_impl<16, true>(tq, tk, tv, tdo, tdk, tdv, a, s) : dkdv_impl<16, false>(tq, tk, tv, tdo, tdk, tdv, a, s);
-    case 32: return causal ? dkdv_impl<32, true>(tq, tk, tv, tdo, tdk, tdv, a, s) : dkdv_impl<32, false>(tq, tk, tv, tdo, tdk, tdv, a, s);
-    case 64: return causal ? dkdv_impl<64, true>(tq, tk, tv, tdo, tdk, tdv, a, s) : dkdv_impl<64, false>(tq, tk, tv, tdo, tdk, tdv, a, s);
-    case 128: return causal ? dkdv_impl<128, true>(tq, tk, tv, tdo, tdk, tdv, a, s) : dkdv_impl<128, false>(tq, tk, tv, tdo, tdk, tdv, a, s);
-    default: return cudaErrorInvalidValue;
-  }
+  return split_dispatch<false>(D, causal, variant, tq, tk, tv, tdo, tdk, tdv, a, s);
 }
 
 cudaError_t launch_bwd_fused_f16(int D, bool causal, const CUtensorMap& tq, const CUtensorMap& tk,

@@ -11,6 +11,7 @@
 #include "../../include/tattn.h"
 #include "common.cuh"
 #include "kernels.h"
+#include "tiles.h"
 
 namespace tattn {
 namespace {
@@ -153,8 +154,10 @@ extern "C" int tattn_fwd(const void* q, const void* k, const void* v, void* o, f
                          int Z, int H, int N, int D, int dtype, int causal, float sm_scale, int tile_cfg,
                          void* stream) {
   if (!strides || !valid_dims(Z, H, N, D) || (dtype != TATTN_F16 && dtype != TATTN_F32) || tile_cfg < 0 ||
-      tile_cfg >= tattn_tile_configs(0))
+      tile_cfg > kNumFwdTiles)
     return TATTN_ERR_INVALID_ARGUMENT;
+  const int variant = tile_cfg == 0 ? tile_default(0, D, causal != 0) : tile_cfg - 1;
+  if (dtype == TATTN_F16 && !tile_supported(0, variant, D)) return TATTN_ERR_UNSUPPORTED;
   if (int64_t(Z) * H * N == 0) return TATTN_OK;
   if (!q || !k || !v || !o || !m) return TATTN_ERR_INVALID_ARGUMENT;
   DeviceState* st;
@@ -183,11 +186,11 @@ extern "C" int tattn_fwd(const void* q, const void* k, const void* v, void* o, f
   a.qk_scale = (sm_scale < 0.f ? -sm_scale : sm_scale) * kLog2e;
   a.negate_s = sm_scale < 0.f ? 1 : 0;
   CUtensorMap tq, tk, tv;
-  const int kv_rows = fwd_f16_kv_rows(D);  // must match the kernel's K/V shared-memory slots
+  const int kv_rows = fwd_f16_kv_rows(D, variant);  // must match the kernel's K/V shared-memory slots
   if ((rc = encode_f16(&tq, q, sq, Z, H, N, D, 128)) != TATTN_OK) return rc;
   if ((rc = encode_f16(&tk, k, sk, Z, H, N, D, kv_rows)) != TATTN_OK) return rc;
   if ((rc = encode_f16(&tv, v, sv, Z, H, N, D, kv_rows)) != TATTN_OK) return rc;
-  return cuda_rc(launch_fwd_f16(D, causal != 0, tile_cfg, tq, tk, tv, a, s));
+  return cuda_rc(launch_fwd_f16(D, causal != 0, variant, tq, tk, tv, a, s));
 }
 
 extern "C" int tattn_bwd_preprocess(const void* o, const void* dout, float* delta, const int64_t* strides, int Z,
@@ -229,8 +232,10 @@ int bwd_common(bool dq_pass, const void* q, const void* k, const void* v, const 
                void* dv, const float* m, const float* delta, const int64_t* strides, int Z, int H, int N, int D,
                int dtype, int causal, float sm_scale, int tile_cfg, void* stream) {
   if (!strides || !valid_dims(Z, H, N, D) || (dtype != TATTN_F16 && dtype != TATTN_F32) || tile_cfg < 0 ||
-      tile_cfg >= tattn_tile_configs(1))
+      tile_cfg > kNumBwdTiles)
     return TATTN_ERR_INVALID_ARGUMENT;
+  const int variant = tile_cfg == 0 ? tile_default(1, D, causal != 0) : tile_cfg - 1;
+  if (dtype == TATTN_F16 && !tile_supported(1, variant, D)) return TATTN_ERR_UNSUPPORTED;
   if (int64_t(Z) * H * N == 0) return TATTN_OK;
   if (!q || !k || !v || !dout || !m || !delta) return TATTN_ERR_INVALID_ARGUMENT;
   if (dq_pass ? !dq : (!dk || !dv)) return TATTN_ERR_INVALID_ARGUMENT;
@@ -268,9 +273,10 @@ int bwd_common(bool dq_pass, const void* q, const void* k, const void* v, const 
   if ((reinterpret_cast<uintptr_t>(dq_pass ? dq : dk) & 15u) != 0 || (!dq_pass && (reinterpret_cast<uintptr_t>(dv) & 15u)))
     return TATTN_ERR_LAYOUT;
   CUtensorMap tq, tk, tv, tdo;
-  // dQ: query tiles of 128 rows, key blocks of 64 rows; dK/dV: key tiles of 128 rows, query blocks of 64.
+  // dQ: query tiles of 128 rows, key blocks of the variant's block_n rows; dK/dV: key tiles of 128 rows,
+  // query blocks of block_n rows.
   int q_rows = 0, kv_rows = 0;
-  bwd_f16_box_rows(D, dq_pass, &q_rows, &kv_rows);  // must match the kernels' shared-memory slots
+  bwd_f16_box_rows(D, dq_pass, variant, &q_rows, &kv_rows);  // must match the kernels' shared-memory slots
   if ((rc = encode_f16(&tq, q, a.sq, Z, H, N, D, q_rows)) != TATTN_OK) return rc;
   if ((rc = encode_f16(&tk, k, a.sk, Z, H, N, D, kv_rows)) != TATTN_OK) return rc;
   if ((rc = encode_f16(&tv, v, a.sv, Z, H, N, D, kv_rows)) != TATTN_OK) return rc;
@@ -281,12 +287,12 @@ int bwd_common(bool dq_pass, const void* q, const void* k, const void* v, const 
   if (dq_pass) {
     CUtensorMap tdq;
     if ((rc = encode_f16(&tdq, dq, dense, Z, H, N, D, kBwdStoreRows, D <= 64 ? D / 2 : 0)) != TATTN_OK) return rc;
-    return cuda_rc(launch_bwd_dq_f16(D, causal != 0, tile_cfg, tq, tk, tv, tdo, tdq, a, s));
+    return cuda_rc(launch_bwd_dq_f16(D, causal != 0, variant, tq, tk, tv, tdo, tdq, a, s));
   }
   CUtensorMap tdk, tdv;
   if ((rc = encode_f16(&tdk, dk, dense, Z, H, N, D, kBwdStoreRows, D <= 64 ? D / 2 : 0)) != TATTN_OK) return rc;
   if ((rc = encode_f16(&tdv, dv, dense, Z, H, N, D, kBwdStoreRows, D <= 64 ? D / 2 : 0)) != TATTN_OK) return rc;
-  return cuda_rc(launch_bwd_dkdv_f16(D, causal != 0, tile_cfg, tq, tk, tv, tdo, tdk, tdv, a, s));
+  return cuda_rc(launch_bwd_dkdv_f16(D, causal != 0, variant, tq, tk, tv, tdo, tdk, tdv, a, s));
 }
 
 }  // namespace
@@ -427,7 +433,29 @@ extern "C" int tattn_layout_ok(const void* ptr, const int64_t* strides, int Z, i
   return layout_ok(ptr, load_strides(strides), Z, H, N, D) ? 1 : 0;
 }
 
-extern "C" int tattn_tile_configs(int kind) { return kind == 0 || kind == 1 ? 1 : 0; }
+extern "C" int tattn_tile_configs(int kind) { return kind == 0 ? kNumFwdTiles : kind == 1 ? kNumBwdTiles : 0; }
+
+extern "C" int tattn_tile_config_info(int kind, int tile_cfg, int* block_m, int* block_n, int* stages) {
+  if (!block_m || !block_n || !stages || tile_cfg < 1 || tile_cfg > tattn_tile_configs(kind))
+    return TATTN_ERR_INVALID_ARGUMENT;
+  const TileVariant& t = kind == 0 ? kFwdTiles[tile_cfg - 1] : kBwdTiles[tile_cfg - 1];
+  *block_m = t.block_m;
+  *block_n = t.block_n;
+  *stages = t.stages;
+  return TATTN_OK;
+}
+
+extern "C" int tattn_tile_default(int kind, int D, int causal, int dtype) {
+  if ((kind != 0 && kind != 1) || (D != 16 && D != 32 && D != 64 && D != 128)) return -1;
+  if (dtype == TATTN_F32) return 0;
+  if (dtype != TATTN_F16) return -1;
+  return tile_default(kind, D, causal != 0) + 1;
+}
+
+extern "C" int tattn_tile_supported(int kind, int tile_cfg, int D) {
+  if (tile_cfg == 0) return (D == 16 || D == 32 || D == 64 || D == 128) ? 1 : 0;
+  return tile_supported(kind, tile_cfg - 1, D) ? 1 : 0;
+}
 
 extern "C" int tattn_device_status(void* stream, int* out, int clear) {
   if (!out) return TATTN_ERR_INVALID_ARGUMENT;

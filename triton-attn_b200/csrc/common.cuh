@@ -339,6 +339,28 @@ __device__ __forceinline__ void tmem_store_cols(uint32_t taddr, const uint32_t* 
 }
 
 // ----------------------------------------------------------------------------------------------
+// CTA order of one-tile-per-CTA causal grids
+// ----------------------------------------------------------------------------------------------
+// Causal tiles differ in cost, so the grid runs them longest first and the hardware's CTA dispatch
+// balances the rest. Longest first across all heads, though, spreads the CTAs running at any time over
+// as many heads as there are SMs, and every CTA streams its head's whole K/V (or Q/dO): with 1,024 heads
+// that working set is far beyond L2 and each CTA reads it from DRAM. So heads are grouped so that one
+// group's K and V (2 * N * D fp16 each) take at most ~48 MiB, and the order is longest first within a
+// group, one group after another. Returns the CTA's position in its head's longest-first order (0 = the
+// longest tile) and sets *bh.
+__device__ __forceinline__ int causal_cta_rank(int nct, int zh, int N, int D, int* bh) {
+  const long long per_head = 4ll * N * D;
+  const int hg = int(per_head <= 0 ? zh : max(1ll, min((long long)zh, (48ll << 20) / per_head)));
+  const int per_group = hg * nct;
+  const int grp = int(blockIdx.x) / per_group;
+  const int h0 = grp * hg;
+  const int gh = min(hg, zh - h0);             // heads in this group (the last one may be short)
+  const int r = int(blockIdx.x) - grp * per_group;  // < gh * nct
+  *bh = h0 + r % gh;
+  return r / gh;
+}
+
+// ----------------------------------------------------------------------------------------------
 // Math
 // ----------------------------------------------------------------------------------------------
 // Hardware base-2 exponential (MUFU). exp2(-inf) = +0.

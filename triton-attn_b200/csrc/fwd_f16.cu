@@ -23,6 +23,7 @@
 // more than kRescaleThreshold (log2 units); P values stay below 2^kRescaleThreshold, exact in fp16.
 #include "common.cuh"
 #include "kernels.h"
+#include "tiles.h"
 
 namespace tattn {
 namespace {
@@ -36,11 +37,12 @@ constexpr int kEmuPairs = 2;
 constexpr int kSoftmaxRegs = 216;
 constexpr int kProducerRegs = 56;
 
-template <int D>
+// Geometry of one tile variant (tiles.h, kFwdTiles): head dim D, BN_ keys per block, NS_ ring stages.
+template <int D, int BN_, int NS_>
 struct FwdCfg {
   static constexpr int BM = 128;                        // rows per query tile (2 tiles per CTA)
-  static constexpr int BN = D == 128 ? 64 : 128;        // keys per block
-  static constexpr int NS = 4;                          // K/V ring depth
+  static constexpr int BN = BN_;                        // keys per block
+  static constexpr int NS = NS_;                        // K/V ring depth
   static constexpr int CW = D < 64 ? D : 64;            // columns per swizzle chunk
   static constexpr int NCH = D / CW;                    // chunks per row (2 for D = 128)
   static constexpr int SWB = CW * 2;                    // swizzle span in bytes (32/64/128)
@@ -70,9 +72,8 @@ struct FwdCfg {
 
 // S_i = Q_i K^T for the K block in ring stage ST: D/16 MMAs (K = 16 each). All descriptor offsets are
 // compile-time constants added to loop-invariant base descriptors.
-template <int D, int ST>
+template <typename C, int D, int ST>
 __device__ __forceinline__ void issue_qk_st(int i, uint32_t d_tmem, uint64_t dQ, uint64_t dK, uint32_t idesc) {
-  using C = FwdCfg<D>;
   // Opaque copies: keep the compiler from hoisting every stage's descriptors into registers.
   asm volatile("" : "+l"(dQ), "+l"(dK));
   const uint64_t a0 = i ? dQ + uint64_t(C::QTILE >> 4) : dQ;
@@ -83,37 +84,38 @@ __device__ __forceinline__ void issue_qk_st(int i, uint32_t d_tmem, uint64_t dQ,
                      dK + uint64_t((ST * C::KTILE + col * C::KCHUNK + inner) >> 4), idesc, kk > 0 ? 1u : 0u);
   }
 }
-template <int D>
+// Ring stage `st` (runtime) to the stage-specialised issue (compile-time offsets).
+template <typename C, int D, int ST = 0>
 __device__ __forceinline__ void issue_qk_stage(int st, int i, uint32_t d_tmem, uint64_t dQ, uint64_t dK,
                                                uint32_t idesc) {
-  static_assert(FwdCfg<D>::NS == 4, "stage dispatch");
-  switch (st) {
-    case 0: issue_qk_st<D, 0>(i, d_tmem, dQ, dK, idesc); break;
-    case 1: issue_qk_st<D, 1>(i, d_tmem, dQ, dK, idesc); break;
-    case 2: issue_qk_st<D, 2>(i, d_tmem, dQ, dK, idesc); break;
-    default: issue_qk_st<D, 3>(i, d_tmem, dQ, dK, idesc); break;
+  if constexpr (ST + 1 < C::NS) {
+    if (st != ST) {
+      issue_qk_stage<C, D, ST + 1>(st, i, d_tmem, dQ, dK, idesc);
+      return;
+    }
   }
+  issue_qk_st<C, D, ST>(i, d_tmem, dQ, dK, idesc);
 }
 
 // O_i += P_i V for the V block in ring stage ST: BN/16 MMAs with P (fp16) read from TMEM.
-template <int D, int ST>
+template <typename C, int D, int ST>
 __device__ __forceinline__ void issue_pv_st(uint32_t d_tmem, uint32_t p_tmem, uint64_t dV, uint32_t accumulate) {
-  using C = FwdCfg<D>;
   asm volatile("" : "+l"(dV));
 #pragma unroll
   for (int kk = 0; kk < C::BN / 16; ++kk)
     mma_f16_ts_elect(d_tmem, p_tmem + kk * 8, dV + uint64_t((ST * C::KTILE + kk * 16 * C::SWB) >> 4), C::IDESC_PV,
                      kk > 0 ? 1u : accumulate);
 }
-template <int D>
+template <typename C, int D, int ST = 0>
 __device__ __forceinline__ void issue_pv_stage(int st, uint32_t d_tmem, uint32_t p_tmem, uint64_t dV,
                                                uint32_t accumulate) {
-  switch (st) {
-    case 0: issue_pv_st<D, 0>(d_tmem, p_tmem, dV, accumulate); break;
-    case 1: issue_pv_st<D, 1>(d_tmem, p_tmem, dV, accumulate); break;
-    case 2: issue_pv_st<D, 2>(d_tmem, p_tmem, dV, accumulate); break;
-    default: issue_pv_st<D, 3>(d_tmem, p_tmem, dV, accumulate); break;
+  if constexpr (ST + 1 < C::NS) {
+    if (st != ST) {
+      issue_pv_stage<C, D, ST + 1>(st, d_tmem, p_tmem, dV, accumulate);
+      return;
+    }
   }
+  issue_pv_st<C, D, ST>(d_tmem, p_tmem, dV, accumulate);
 }
 
 // Max of one row of raw scores; MASK ignores columns >= lim.
@@ -162,11 +164,11 @@ __device__ __forceinline__ float exp_cols(const uint32_t* s, uint32_t* p, uint64
   return t.x + t.y;
 }
 
-template <int D, bool CAUSAL>
+template <int D, bool CAUSAL, int BN_, int NS_>
 __global__ void __launch_bounds__(384, 1)
     fwd_f16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const FwdArgs args) {
-  using C = FwdCfg<D>;
+  using C = FwdCfg<D, BN_, NS_>;
   constexpr int BN = C::BN;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
@@ -192,9 +194,8 @@ __global__ void __launch_bounds__(384, 1)
   const int N = args.N;
   const int nct = (N + 2 * C::BM - 1) / (2 * C::BM);  // CTAs per (z, h)
   int bh, cta;
-  if (CAUSAL) {  // longest-first: all heads' heaviest row blocks are scheduled first
-    bh = blockIdx.x % (args.Z * args.H);
-    cta = nct - 1 - blockIdx.x / (args.Z * args.H);
+  if (CAUSAL) {  // longest first within groups of heads whose K/V fit in L2 (the highest row blocks see the most keys)
+    cta = nct - 1 - causal_cta_rank(nct, args.Z * args.H, N, D, &bh);
   } else {  // row blocks of one head adjacent: K/V of a head stay hot in L2
     bh = blockIdx.x / nct;
     cta = blockIdx.x % nct;
@@ -294,7 +295,7 @@ __global__ void __launch_bounds__(384, 1)
       bool ok = n > 0 && warp_wait(bar_q, 0, ab) && warp_wait(&bar_k_full[0], 0, ab);
       if (ok) {
         tc_fence_after();
-        issue_qk_stage<D>(0, i, tS, dQ, dK, idesc_s);
+        issue_qk_stage<C, D>(0, i, tS, dQ, dK, idesc_s);
         mma_commit_elect(&bar_s_full[i]);
       }
       for (int j = 0; ok && j < n; ++j) {
@@ -305,7 +306,7 @@ __global__ void __launch_bounds__(384, 1)
             break;
           }
           tc_fence_after();
-          issue_qk_stage<D>(b % C::NS, i, tS, dQ, dK, idesc_s);
+          issue_qk_stage<C, D>(b % C::NS, i, tS, dQ, dK, idesc_s);
           mma_commit_elect(&bar_s_full[i]);
         }
         if (!warp_wait(&bar_p_full[i], j & 1, ab) || !warp_wait(&bar_v_full[j % C::NS], (j / C::NS) & 1, ab)) {
@@ -313,7 +314,7 @@ __global__ void __launch_bounds__(384, 1)
           break;
         }
         tc_fence_after();
-        issue_pv_stage<D>(j % C::NS, tO, tP, dV, j > 0 ? 1u : 0u);
+        issue_pv_stage<C, D>(j % C::NS, tO, tP, dV, j > 0 ? 1u : 0u);
         mma_commit_elect(&bar_o_done[i]);
         mma_commit_elect(&bar_kv_empty[i * C::NS + j % C::NS]);
       }
@@ -442,11 +443,11 @@ __global__ void __launch_bounds__(384, 1)
   }
 }
 
-template <int D, bool CAUSAL>
+template <int D, bool CAUSAL, int BN, int NS>
 cudaError_t launch_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const FwdArgs& a,
                         cudaStream_t s) {
-  using C = FwdCfg<D>;
-  auto kern = fwd_f16_kernel<D, CAUSAL>;
+  using C = FwdCfg<D, BN, NS>;
+  auto kern = fwd_f16_kernel<D, CAUSAL, BN, NS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   if (e != cudaSuccess) return e;
   const int nct = (a.N + 2 * C::BM - 1) / (2 * C::BM);
@@ -457,24 +458,40 @@ cudaError_t launch_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUte
   return cudaGetLastError();
 }
 
-}  // namespace
-
-int fwd_f16_kv_rows(int D) {
-  switch (D) {
-    case 16: return FwdCfg<16>::BN;
-    case 32: return FwdCfg<32>::BN;
-    case 64: return FwdCfg<64>::BN;
-    case 128: return FwdCfg<128>::BN;
-    default: return 0;
+// Variant v (tiles.h, kFwdTiles) for head dim D; variants whose blocks do not fit D's TMEM budget are
+// not instantiated.
+template <int D, bool CAUSAL>
+cudaError_t launch_variant(int v, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                           const FwdArgs& a, cudaStream_t s) {
+  static_assert(kNumFwdTiles == 3, "variant dispatch");
+  switch (v) {
+    case 0:
+      if constexpr (D <= 64) return launch_impl<D, CAUSAL, kFwdTiles[0].block_n, kFwdTiles[0].stages>(tq, tk, tv, a, s);
+      break;
+    case 1:
+      return launch_impl<D, CAUSAL, kFwdTiles[1].block_n, kFwdTiles[1].stages>(tq, tk, tv, a, s);
+    case 2:
+      if constexpr (D <= 64) return launch_impl<D, CAUSAL, kFwdTiles[2].block_n, kFwdTiles[2].stages>(tq, tk, tv, a, s);
+      break;
+    default:
+      break;
   }
+  return cudaErrorNotSupported;
 }
 
-cudaError_t launch_fwd_f16(int D, bool causal, int tile_cfg, const CUtensorMap& tq, const CUtensorMap& tk,
+}  // namespace
+
+int fwd_f16_kv_rows(int D, int variant) {
+  return tile_supported(0, variant, D) ? kFwdTiles[variant].block_n : 0;
+}
+
+cudaError_t launch_fwd_f16(int D, bool causal, int variant, const CUtensorMap& tq, const CUtensorMap& tk,
                            const CUtensorMap& tv, const FwdArgs& a, cudaStream_t s) {
-  (void)tile_cfg;  // one tile shape per head dim for now
-#define TATTN_FWD_CASE(DD)                                                         \
-  case DD:                                                                         \
-    return causal ? launch_impl<DD, true>(tq, tk, tv, a, s) : launch_impl<DD, false>(tq, tk, tv, a, s);
+  if (!tile_supported(0, variant, D)) return cudaErrorNotSupported;
+#define TATTN_FWD_CASE(DD)                                                                     \
+  case DD:                                                                                     \
+    return causal ? launch_variant<DD, true>(variant, tq, tk, tv, a, s)                        \
+                  : launch_variant<DD, false>(variant, tq, tk, tv, a, s);
   switch (D) {
     TATTN_FWD_CASE(16)
     TATTN_FWD_CASE(32)

@@ -41,22 +41,24 @@ struct BwdArgs {
   unsigned long long wait_limit_ns;  // bound of every mbarrier wait (tattn_set_wait_limit_ns)
 };
 
-// Rows per K/V block of the fp16 forward for head dim D: the TMA box height of its K and V tensor maps
-// (the Q map always uses 128-row boxes). The kernel's shared-memory slots are sized for exactly this.
-int fwd_f16_kv_rows(int D);
-// TMA box heights of the fp16 backward kernels' Q/dO and K/V tensor maps for head dim D (dQ pass or
-// dK/dV pass).
-void bwd_f16_box_rows(int D, bool dq_pass, int* q_rows, int* kv_rows);
+// `variant` below is a 0-based tile variant of tiles.h (kFwdTiles / kBwdTiles); launchers return
+// cudaErrorNotSupported for a variant that does not fit head dim D.
+// Rows per K/V block of the fp16 forward variant for head dim D: the TMA box height of its K and V
+// tensor maps (the Q map always uses 128-row boxes); 0 if the variant does not fit D.
+int fwd_f16_kv_rows(int D, int variant);
+// TMA box heights of the fp16 split-backward kernels' Q/dO and K/V tensor maps for head dim D, dQ pass
+// or dK/dV pass, and tile variant.
+void bwd_f16_box_rows(int D, bool dq_pass, int variant, int* q_rows, int* kv_rows);
 
 // fp16 tcgen05 kernels (tensor maps describe [Z, H, N, D] tensors as 4-D {D, N, H, Z}).
-cudaError_t launch_fwd_f16(int D, bool causal, int tile_cfg, const CUtensorMap& tq, const CUtensorMap& tk,
+cudaError_t launch_fwd_f16(int D, bool causal, int variant, const CUtensorMap& tq, const CUtensorMap& tk,
                            const CUtensorMap& tv, const FwdArgs& a, cudaStream_t s);
 // tdq: store map of the dense dQ output, kBwdStoreRows-row boxes of D/2 columns (D <= 64).
-cudaError_t launch_bwd_dq_f16(int D, bool causal, int tile_cfg, const CUtensorMap& tq, const CUtensorMap& tk,
+cudaError_t launch_bwd_dq_f16(int D, bool causal, int variant, const CUtensorMap& tq, const CUtensorMap& tk,
                               const CUtensorMap& tv, const CUtensorMap& tdo, const CUtensorMap& tdq, const BwdArgs& a,
                               cudaStream_t s);
 // tdk / tdv: store maps of the dense dK / dV outputs, kBwdStoreRows-row boxes of D/2 columns (D <= 64).
-cudaError_t launch_bwd_dkdv_f16(int D, bool causal, int tile_cfg, const CUtensorMap& tq, const CUtensorMap& tk,
+cudaError_t launch_bwd_dkdv_f16(int D, bool causal, int variant, const CUtensorMap& tq, const CUtensorMap& tk,
                                 const CUtensorMap& tv, const CUtensorMap& tdo, const CUtensorMap& tdk,
                                 const CUtensorMap& tdv, const BwdArgs& a, cudaStream_t s);
 // Fused backward (dK, dV and dQ in one kernel; D <= 64, causal or not): tq/tdo with 128-row boxes, tk/tv

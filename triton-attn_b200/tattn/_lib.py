@@ -35,6 +35,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tattn_set_wait_limit_ns": (_I, [_U64]),
     "tattn_get_wait_limit_ns": (_U64, []),
     "tattn_tile_configs": (_I, [_I]),
+    "tattn_tile_config_info": (_I, [_I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I)]),
+    "tattn_tile_default": (_I, [_I, _I, _I, _I]),
+    "tattn_tile_supported": (_I, [_I, _I, _I]),
     "tattn_device_status": (_I, [_P, ctypes.POINTER(ctypes.c_int), _I]),
     "tattn_status_string": (ctypes.c_char_p, [_I]),
     "tattn_abi_version": (_I, []),

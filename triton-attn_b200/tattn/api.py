@@ -20,13 +20,25 @@ from torch.autograd.function import once_differentiable
 
 from tattn import _lib
 
-# Tile variants per kernel family, in tile_cfg order (index 0 is the default). They stand in for the
-# reference's autotune spaces (kernels.py:21-41); "BLOCK_M" is the query rows a CTA owns, "BLOCK_N"
-# the keys per inner step.
+# Explicit tile variants per kernel family; TILE_CONFIGS[kind][i] is the library's tile_cfg i + 1
+# (tile_cfg 0 = the library's default for the call's (D, causal, dtype)). They stand in for the
+# reference's autotune spaces (kernels.py:21-41): "BLOCK_M" is the rows a CTA owns (the forward's two
+# 128-row query tiles; the backward's 128-row key or query tile), "BLOCK_N" the rows of each inner block
+# it loops over, "num_stages" the depth of the TMA ring. "bwd" covers the split backward (dK/dV and dQ
+# kernels); the fused backward (the default for fp16, D <= 64) has one shape. This copy of the library's
+# table (csrc/tiles.h) is checked against tattn_tile_config_info by the CPU tests.
 TILE_CONFIGS: dict[str, list[dict[str, int]]] = {
-    "fwd": [{"BLOCK_M": 256, "BLOCK_N": 128}],
-    "bwd": [{"BLOCK_M": 128, "BLOCK_N": 64}],
+    "fwd": [
+        {"BLOCK_M": 256, "BLOCK_N": 128, "num_stages": 4},
+        {"BLOCK_M": 256, "BLOCK_N": 64, "num_stages": 4},
+        {"BLOCK_M": 256, "BLOCK_N": 128, "num_stages": 2},
+    ],
+    "bwd": [
+        {"BLOCK_M": 128, "BLOCK_N": 128, "num_stages": 4},
+        {"BLOCK_M": 128, "BLOCK_N": 64, "num_stages": 4},
+    ],
 }
+_KIND = {"fwd": 0, "bwd": 1}
 
 
 def _check(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
@@ -71,19 +83,27 @@ def _require_cuda(t: torch.Tensor) -> None:
 
 
 def _tile_cfg(config: dict[str, int] | None, kind: str) -> int:
-    """Map a reference-style tile ``config`` (or {"tile_cfg": i}) to the library's tile index."""
+    """Map a reference-style tile ``config`` (its BLOCK_M / BLOCK_N / num_stages keys; others such as
+    num_warps have no meaning here) or {"tile_cfg": i} to the library's tile_cfg (0 = default)."""
     if config is None:
         return 0
     if "tile_cfg" in config:
         idx = int(config["tile_cfg"])
-        if not 0 <= idx < len(TILE_CONFIGS[kind]):
+        if not 0 <= idx <= len(TILE_CONFIGS[kind]):
             raise ValueError(f"tile_cfg {idx} out of range for {kind}")
         return idx
-    want = {key: config[key] for key in ("BLOCK_M", "BLOCK_N") if key in config}
+    want = {key: config[key] for key in ("BLOCK_M", "BLOCK_N", "num_stages") if key in config}
     for idx, cand in enumerate(TILE_CONFIGS[kind]):
         if all(cand.get(key) == val for key, val in want.items()):
-            return idx
+            return idx + 1
     raise ValueError(f"no {kind} tile variant matches {config}; available: {TILE_CONFIGS[kind]}")
+
+
+def tile_supported(config: dict[str, int] | None, kind: str, head_dim: int) -> bool:
+    """Whether the fp16 kernels of family ``kind`` can run ``config`` at ``head_dim`` (the reference
+    prunes configs that do not fit its shared memory, kernels.py:44-54; here TMEM and shared memory
+    decide, and an explicit config that does not fit is an error)."""
+    return bool(_lib.load().tattn_tile_supported(_KIND[kind], _tile_cfg(config, kind), head_dim))
 
 
 def _strides(t: torch.Tensor) -> tuple[int, ...]:
