@@ -58,11 +58,16 @@ STRONG = {"cfg5"}  # configs whose fixed (batch, head) pairs are split over the 
 # (its results/t4.json); it publishes nothing for config 5.
 T4_PUBLISHED = {"cfg2": 16.9, "cfg3": 15.9}
 L2_BYTES = 126 * 2**20
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the fused backward kernel
-# per (batch, head) pair, from an ncu capture of the current build on a 64-pair slice of each config
-# (inputs 5 x 64 MiB > L2), divided by the captured pairs; the summaries under profiles/ give the
-# commands and the raw figures. Scaled by the pairs a launch processes, as traffic grows with them.
-NCU_TRAFFIC_PER_PAIR: dict[tuple[str, str], float] = {}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of each kernel per (batch,
+# head) pair, from an ncu capture of the current build on a 64-pair slice of config 5 (inputs 5 x 64 MiB
+# > L2; the command is NCU_TRAFFIC_SOURCE), divided by the captured pairs. Scaled by the pairs a launch
+# processes, as the traffic grows with them.
+NCU_TRAFFIC_PER_PAIR: dict[tuple[str, str], float] = {
+    ("cfg5", "bwd_fused"): (406_999_296 + 222_435_584) / 64,
+    ("cfg5", "fwd"): (206_485_760 + 50_135_040) / 64,
+}
+NCU_TRAFFIC_SOURCE = ("ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum --clock-control none "
+                      "-k regex:'bwd_fused|fwd_f16' -s 6 -c 2 python bench.py --lean --pairs 64 --steps 2 --warmup 3")
 
 
 def flops(b: int, h: int, n: int, d: int, causal: bool, mode: str) -> float:
@@ -611,7 +616,11 @@ def run_gpu(args) -> None:
                 "frac": round(achieved / pk["tflops"], 4),
                 "frac_of_sustained": round(achieved / pk["tflops_sustained"], 4) if pk.get("tflops_sustained") else None,
                 "traffic": round(traffic * pairs) if traffic else None,
-                "algorithmic_bytes": (9 if dom == "bwd_fused" else 4) * pairs * n * d * 2 + 8 * pairs * n,
+                "traffic_source": ("one launch on a 64-pair slice of the config, per pair x the pairs of this "
+                                   "launch: " + NCU_TRAFFIC_SOURCE) if traffic else None,
+                # the op's own tensors: backward reads q, k, v, O, dO, M and writes dq, dk, dv (the fp32 dQ
+                # workspace is the implementation's); forward reads q, k, v and writes O, M
+                "algorithmic_bytes": (8 if dom == "bwd_fused" else 4) * pairs * n * d * 2 + 4 * pairs * n,
                 "flops_per_launch": kflops[dom],
                 "timing": "CUDA events around each call inside the timed steps, mean over steps, max over ranks",
             },
