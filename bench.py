@@ -20,6 +20,9 @@ tiled_forward / tiled_backward in oracle/) on the host cores: each step runs com
 pairs of the same config, one per worker process, every key and query block of them, and the line
 reports their FLOPs over the step's wall time.
 
+``--variants`` (one GPU) times every tile variant of the library's tile table (forward, split backward)
+and the fused backward at configs 2 and 3 and a config-5 slice, one JSON line each.
+
 ``--compare`` (one GPU) prints one JSON line per implementation and config, in the spirit of the
 reference's bench/bench.py comparison table (bench.py:62-76, 128-171): this library, torch's
 scaled_dot_product_attention with each backend (flash, cuDNN, memory-efficient) and a naive
@@ -749,6 +752,45 @@ def run_compare(args) -> None:
             torch.cuda.empty_cache()
 
 
+def run_variants(args) -> None:
+    """Every tile variant of the tile table (tattn.api.TILE_CONFIGS, i.e. the library's csrc/tiles.h) on
+    one GPU, one JSON line each: the forward variants, the split backward (dK/dV + dQ) variants, and the
+    fused backward, at configs 2 and 3 and a 128-pair slice of config 5. This is the evidence behind the
+    default per (D, causal): the same launches under ncu give each variant's tensor-pipe activity."""
+    import torch
+
+    from tattn import _lib, api
+
+    dev = torch.device("cuda", 0)
+    cases = {"cfg2": CONFIGS["cfg2"], "cfg3": CONFIGS["cfg3"], "cfg5_slice128": (8,) + CONFIGS["cfg5"][1:]}
+    timer = _Timer(1, dev)
+    for name, (b, h, n, d, causal) in cases.items():
+        q, k, v, do = (t.view(b, h, n, d) for t in _inputs(b * h, n, d, dev, 77))
+        sc = 1.0 / math.sqrt(d)
+        f = flops(b, h, n, d, causal, "fwd")
+        o, m = api._forward(q, k, v, causal, sc)
+        runs = [("fwd", i + 1, cfg, lambda cfg=cfg: api._forward(q, k, v, causal, sc, config=cfg), f)
+                for i, cfg in enumerate(api.TILE_CONFIGS["fwd"]) if api.tile_supported(cfg, "fwd", d)]
+        runs += [("bwd_split", i + 1, cfg, lambda cfg=cfg: api._backward(q, k, v, o, m, do, causal, sc, config=cfg),
+                  2.5 * f) for i, cfg in enumerate(api.TILE_CONFIGS["bwd"]) if api.tile_supported(cfg, "bwd", d)]
+        runs.append(("bwd_fused", 0, {}, lambda: api._backward(q, k, v, o, m, do, causal, sc), 2.5 * f))
+        for kind, idx, cfg, fn, fl in runs:
+            for _ in range(args.warmup):
+                fn()
+            ms = timer(fn, args.steps) / args.steps
+            # tile_cfg 0 of tattn_fwd / the split backward resolves to this variant; the API's fp16 backward
+            # for D <= 64 is the fused kernel
+            default = _lib.load().tattn_tile_default(api._KIND["fwd" if kind == "fwd" else "bwd"], d, int(causal), 0)
+            print(json.dumps({"variants": name, "kind": kind, "tile_cfg": idx, **cfg, "ms": round(ms, 4),
+                              "tflops": round(fl / (ms * 1e-3) / 1e12, 1),
+                              "default": kind == "bwd_fused" or idx == default}),
+                  flush=True)  # fmt: skip
+        del q, k, v, do, o, m
+        torch.cuda.empty_cache()
+    if _lib.device_status() != 0:
+        raise RuntimeError("device status word set during the variant sweep")
+
+
 def run_reference(args) -> None:
     """The reference's CPU implementation of the path (oracle restatement), rank 0 only: W warm-up steps,
     then K timed steps, each `workers` complete (batch, head) pairs of the config in parallel."""
@@ -809,11 +851,15 @@ def main() -> None:
     ap.add_argument("--lean", action="store_true", help="warm-up + timed steps only (for profiler runs)")
     ap.add_argument("--compare", action="store_true",
                     help="comparison table against torch SDPA backends and a naive softmax (one GPU)")
+    ap.add_argument("--variants", action="store_true", help="time every tile variant of the tile table (one GPU)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.compare:
         run_compare(args)
+        return
+    if args.variants:
+        run_variants(args)
         return
     if args.impl == "reference":
         run_reference(args)
