@@ -762,7 +762,8 @@ def run_variants(args) -> None:
     from tattn import _lib, api
 
     dev = torch.device("cuda", 0)
-    cases = {"cfg2": CONFIGS["cfg2"], "cfg3": CONFIGS["cfg3"], "cfg5_slice128": (8,) + CONFIGS["cfg5"][1:]}
+    cases = {"cfg2": CONFIGS["cfg2"], "cfg3": CONFIGS["cfg3"], "cfg5_slice128": (8,) + CONFIGS["cfg5"][1:],
+             "cfg2_d128": (4, 16, 4096, 128, False), "cfg2_d128_causal": (4, 16, 4096, 128, True)}
     timer = _Timer(1, dev)
     for name, (b, h, n, d, causal) in cases.items():
         q, k, v, do = (t.view(b, h, n, d) for t in _inputs(b * h, n, d, dev, 77))
