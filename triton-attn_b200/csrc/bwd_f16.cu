@@ -35,6 +35,8 @@
 // and each barrier wait or commit costs it a hundred cycles or more, so one issuer would serialise the
 // S/dP MMAs of one block behind the accumulating MMAs of another. A ring slot is released when both
 // commits for it (S/dP and accumulation) have landed.
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "tiles.h"
@@ -1678,8 +1680,17 @@ struct FusedCfg {
   static constexpr int OFF_DO = OFF_Q + NS * T_Q;         // NS dO blocks
   static constexpr int OFF_DS = OFF_DO + NS * T_Q;        // dS^T of the current block
   static constexpr int OFF_STG = OFF_DS + T_DS;           // 8 compute warps x STG
-  static constexpr int OFF_MD = OFF_STG + 8 * STG;        // NS x (BQ -M | BQ -delta) fp32
-  static constexpr int OFF_BAR = OFF_MD + NS * 2 * BQ * 4;
+  // -M/qk_scale and -delta of each query of a ring slot, each as an exact sum of three bf16 parts, as
+  // the B operand [128 queries x 16 K] (no swizzle; K columns 0-2 = the -M parts, 3-5 = the -delta
+  // parts, 6-7 zero) of one extra K = 16 step of the S^T and dP^T MMAs. Only 8 K columns are stored: the
+  // step's upper 8 read the same bytes (LBO = 0), against zeros in the A operand.
+  static constexpr int MD_SLOT = BQ * 16;
+  static constexpr int OFF_MD = OFF_STG + 8 * STG;        // NS x MD_SLOT
+  // The A operands of that step, [128 keys x 16 K] bf16 (no swizzle): ones in K columns 0-2 (S^T) or
+  // 3-5 (dP^T), zeros elsewhere, so the step adds -M/qk_scale to S^T and -delta to dP^T.
+  static constexpr int ONES_TILE = 128 * 32;
+  static constexpr int OFF_ONES = OFF_MD + NS * MD_SLOT;  // 2 x ONES_TILE
+  static constexpr int OFF_BAR = OFF_ONES + 2 * ONES_TILE;
   // k_full[2], k_empty[2], q_full[NS], md_full[NS], q_empty[NS], s_full, s_free, p_full, acc_free,
   // acc_done, acc_read, fin[3], dq_read, v_full, v_empty
   static constexpr int NBARS = 4 + 3 * NS + 12;
@@ -1689,11 +1700,45 @@ struct FusedCfg {
   static constexpr uint32_t T_ST = 0, T_DPT = 128, T_PT = 256, T_DV = 320, T_DK = 320 + D, T_DQ = 320 + 2 * D;
   static_assert(T_DQ + D <= 512, "TMEM budget");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
-  static_assert(OFF_DS % 1024 == 0 && OFF_STG % 1024 == 0, "alignment");
+  static_assert(OFF_DS % 1024 == 0 && OFF_STG % 1024 == 0 && OFF_MD % 128 == 0 && OFF_ONES % 128 == 0,
+                "alignment");
   static constexpr uint32_t IDESC_S = idesc_f16_f32(128, BQ, false);
   static constexpr uint32_t IDESC_ACC = idesc_f16_f32(128, D, true);     // A K-major, B MN-major
   static constexpr uint32_t IDESC_DQ = idesc_f16_f32_amn(128, D, true);  // A (dS) and B (K) MN-major
+  static constexpr uint32_t IDESC_MD = idesc_f16_f32(128, BQ, false) | (1u << 7) | (1u << 10);  // bf16 A, B
 };
+
+// v as the sum of three bf16 values (exact: each step leaves at most 8 fewer significant bits).
+__device__ __forceinline__ void split_bf16x3(float v, uint32_t* h) {
+  const __nv_bfloat16 a = __float2bfloat16_rn(v);
+  const float r1 = v - __bfloat162float(a);
+  const __nv_bfloat16 b = __float2bfloat16_rn(r1);
+  const float r2 = r1 - __bfloat162float(b);
+  const __nv_bfloat16 c = __float2bfloat16_rn(r2);
+  h[0] = __bfloat16_as_ushort(a);
+  h[1] = __bfloat16_as_ushort(b);
+  h[2] = __bfloat16_as_ushort(c);
+}
+
+// P^T and dS^T for H query columns of one key row of the fused backward, whose S^T and dP^T already hold
+// S^T - M/qk_scale and dP^T - delta (folded into the MMAs): P = exp2(S'^T * qk_scale), dS = P * dP'^T.
+// MASK keeps only columns c_lo <= c < c_hi.
+template <int H, bool MASK>
+__device__ __forceinline__ void pds_row_folded(const uint32_t* s, const uint32_t* dp, uint32_t* pt, uint32_t* dst,
+                                               uint64_t scale2, int c_lo, int c_hi) {
+#pragma unroll
+  for (int c = 0; c < H; c += 2) {
+    const uint64_t x = fmul2(f2(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), scale2);
+    float2 e = (((c / 2) & 7) < kDkvEmuPairs) ? exp2_pair<true>(x) : exp2_pair<false>(x);
+    if (MASK) {
+      e.x = (c >= c_lo && c < c_hi) ? e.x : 0.f;
+      e.y = (c + 1 >= c_lo && c + 1 < c_hi) ? e.y : 0.f;
+    }
+    pt[c / 2] = pack_half2(e.x, e.y);
+    const float2 v = f2_unpack(fmul2(f2(e.x, e.y), f2(__uint_as_float(dp[c]), __uint_as_float(dp[c + 1]))));
+    dst[c / 2] = pack_half2(v.x, v.y);
+  }
+}
 
 // Add the warp's part of a block's dQ partial (32 query rows x D/2 fp32 columns, in registers) into the
 // fp32 workspace at (col, row) through the warp's staging area.
@@ -1746,7 +1791,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bar_dq_read = bar_s_full + 9;       // the compute warps hold the previous block's dQ part
   uint64_t* bar_v_full = bar_s_full + 10;       // value tile landed
   uint64_t* bar_v_empty = bar_s_full + 11;      // every dP^T MMA of the value tile's tile has completed
-  float* md = reinterpret_cast<float*>(smem + C::OFF_MD);
+  uint8_t* md = smem + C::OFF_MD;  // per ring slot: [BQ queries x 16 B] bf16 parts of -M/qk_scale, -delta
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
   const CtaAbort ab{abort_flag, args.status, args.wait_limit_ns};
@@ -1820,6 +1865,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tm_v);
     tma_prefetch_desc(&tm_do);
   }
+  // The constant A operands of the folded -M / -delta step (bf16 1.0 = 0x3F80): in every 8-row group,
+  // bytes [0, 128) hold K columns 0-7 of the 8 rows (16 bytes a row), bytes [128, 256) columns 8-15.
+  for (int idx = threadIdx.x; idx < 2 * C::ONES_TILE / 16; idx += blockDim.x) {
+    const int t = idx / (C::ONES_TILE / 16), byte = (idx % (C::ONES_TILE / 16)) * 16;
+    const bool low_k = (byte % 256) < 128;
+    const uint4 row = t == 0 ? make_uint4(0x3F803F80u, 0x00003F80u, 0u, 0u)   // K 0-2: the -M parts
+                             : make_uint4(0u, 0x3F800000u, 0x3F803F80u, 0u);  // K 3-5: the -delta parts
+    *reinterpret_cast<uint4*>(smem + C::OFF_ONES + t * C::ONES_TILE + byte) = low_k ? row : make_uint4(0u, 0u, 0u, 0u);
+  }
+  fence_proxy_async_smem();  // the tensor core reads them through the async proxy
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -1847,6 +1902,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++kv_issued;
         const float* mrow = args.m + int64_t(bh) * N;
         const float* drow = args.delta + int64_t(bh) * N;
+        const float inv_scale = 1.f / args.qk_scale;  // qk_scale > 0 here (the host takes sm_scale = 0 elsewhere)
         for (int c = 0; c < n; ++c, ++g) {
           const int st = g % NS;
           if (g >= NS && !warp_wait(&bar_q_empty[st], ((g / NS) - 1) & 1, ab)) { ok = false; break; }
@@ -1858,13 +1914,18 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_4d(sDO + st * C::T_Q + ch * G::chunk(BQ), &tm_do, ch * G::CW, qr, hi, zi, &bar_q_full[st]);
             }
           }
-          float* slot = md + st * 2 * BQ;
+          // Query j's 16 bytes: bf16 parts of -M/qk_scale (K 0-2) and of -delta (K 3-5), zeros (K 6-7).
+          uint8_t* slot = md + st * C::MD_SLOT;
 #pragma unroll
           for (int j = lane; j < BQ; j += 32) {
             const int q = qr + j;
-            slot[j] = q < N ? -mrow[q] : 0.f;
-            slot[BQ + j] = q < N ? -drow[q] : 0.f;
+            uint32_t hm[3], hd[3];
+            split_bf16x3(q < N ? -mrow[q] * inv_scale : 0.f, hm);
+            split_bf16x3(q < N ? -drow[q] : 0.f, hd);
+            *reinterpret_cast<uint4*>(slot + j * 16) =
+                make_uint4(hm[0] | (hm[1] << 16), hm[2] | (hd[0] << 16), hd[1] | (hd[2] << 16), 0u);
           }
+          fence_proxy_async_smem();  // read by the S^T / dP^T MMAs through the async proxy
           mbar_arrive(&bar_md_full[st]);
         }
       }
@@ -1880,6 +1941,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t dV = smem_desc(sV, 16, 8 * G::SWB, G::LAYOUT);
       const uint64_t dQ = smem_desc(sQ, 16, 8 * G::SWB, G::LAYOUT);
       const uint64_t dDO = smem_desc(sDO, 16, 8 * G::SWB, G::LAYOUT);
+      // The folded step: A = constant ones tiles (K-major, no swizzle: K core matrices 128 bytes apart,
+      // 8-row groups 256), B = the slot's parts (no swizzle: 8-query groups 128 bytes apart, the upper
+      // K core matrix the same bytes).
+      const uint64_t dOnesM = smem_desc(base_u32 + C::OFF_ONES, 128, 256, 0u);
+      const uint64_t dOnesD = smem_desc(base_u32 + C::OFF_ONES + C::ONES_TILE, 128, 256, 0u);
+      const uint64_t dMD = smem_desc(base_u32 + C::OFF_MD, 0, 128, 0u);
       int g = 0, it = 0;
       bool ok = true;
       int2 seq = make_int2(int(blockIdx.x), 0);
@@ -1893,11 +1960,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t ko = uint64_t((kb * C::T_KEY) >> 4);
         for (int c = 0; c < n; ++c, ++g) {
           if (g > 0 && !warp_wait(bar_s_free, (g - 1) & 1, ab)) { ok = false; break; }
-          if (!warp_wait(&bar_q_full[g % NS], (g / NS) & 1, ab)) { ok = false; break; }
+          if (!warp_wait(&bar_q_full[g % NS], (g / NS) & 1, ab) || !warp_wait(&bar_md_full[g % NS], (g / NS) & 1, ab)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
           const uint64_t so = uint64_t(((g % NS) * C::T_Q) >> 4);
+          const uint64_t mo = uint64_t(((g % NS) * C::MD_SLOT) >> 4);
+          // S'^T = S^T - M/qk_scale and dP'^T = dP^T - delta: one more K = 16 step each (bf16, no negation)
           mma_kmajor<D, G::chunk(128), G::chunk(BQ)>(tmem + C::T_ST, dK + ko, dQ + so, idesc_s);
+          mma_f16_ss_elect(tmem + C::T_ST, dOnesM, dMD + mo, C::IDESC_MD, 1u);
           mma_kmajor<D, G::chunk(128), G::chunk(BQ)>(tmem + C::T_DPT, dV, dDO + so, C::IDESC_S);
+          mma_f16_ss_elect(tmem + C::T_DPT, dOnesD, dMD + mo, C::IDESC_MD, 1u);
           mma_commit_elect(bar_s_full);
           mma_commit_elect(&bar_q_empty[g % NS]);
         }
@@ -1993,7 +2067,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int zi = bh / args.H, hi = bh % args.H, k0 = 128 * kt, lo = tile_lo(kt), n = NBq - lo;
       const int key = k0 + r;
       for (int c = 0; c < n; ++c, ++g) {
-        const int st = g % NS;
         if (!warp_wait(bar_s_full, g & 1, ab)) { ok = false; break; }
         tc_fence_after();
         uint32_t s[H], dp[H];
@@ -2004,17 +2077,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         reg_fence<H>(dp);
         tc_fence_before();
         mbar_arrive(bar_s_free);  // the tensor core may now write S^T/dP^T of the next block
-        if (!warp_wait(&bar_md_full[st], (g / NS) & 1, ab)) { ok = false; break; }
-        const float* mq = md + st * 2 * BQ + w * H;
         const int q0 = (lo + c) * BQ + w * H;  // first query column of this warpgroup's half
         const bool masked = (q0 + H > N) || (k0 + 128 > N) || (CAUSAL && q0 < k0 + 127);
         const int c_lo = CAUSAL ? max(0, key - q0) : 0;  // valid query columns: c_lo <= c < c_hi
         const int c_hi = key < N ? N - q0 : 0;
         uint32_t pt[H / 2], dst[H / 2];
         if (masked)
-          pds_row<H, true>(s, dp, mq, mq + BQ, pt, dst, scale2, c_lo, c_hi);
+          pds_row_folded<H, true>(s, dp, pt, dst, scale2, c_lo, c_hi);
         else
-          pds_row<H, false>(s, dp, mq, mq + BQ, pt, dst, scale2, c_lo, c_hi);
+          pds_row_folded<H, false>(s, dp, pt, dst, scale2, c_lo, c_hi);
         if (g > 0) {  // the previous block's dV/dK/dQ MMAs have read P^T and dS^T and written dQ_part
           if (!warp_wait(bar_acc_free, (g - 1) & 1, ab)) { ok = false; break; }
           tc_fence_after();
