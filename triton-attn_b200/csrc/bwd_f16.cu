@@ -963,13 +963,51 @@ __device__ __forceinline__ void pds_row(const uint32_t* s, const uint32_t* dp, c
   }
 }
 
-// TMA producer of the dK/dV kernels (whole warp; lane 0 issues the copies): the CTA's key and value
-// tiles once, then per query block its Q and dO blocks (ring slot c % NS) and -M / -delta of its BQ
-// queries (staged by all lanes into the slot's fp32 area).
+// The scale the folded -M step divides by: qk_scale, but at least 2^-60, so that sm_scale = 0 (or any
+// tinier one) still folds: x = s_eff * (S - M / s_eff) = -M + s_eff * S, and s_eff * S < 2^-60 * |S| is
+// far below an fp32 ulp of M whenever qk_scale is below s_eff. Staging and compute use the same value.
+__device__ __forceinline__ float fold_scale(float qk_scale) { return fmaxf(qk_scale, 0x1p-60f); }
+
+// v as the sum of three bf16 values (exact: each step leaves at most 8 fewer significant bits).
+__device__ __forceinline__ void split_bf16x3(float v, uint32_t* h) {
+  const __nv_bfloat16 a = __float2bfloat16_rn(v);
+  const float r1 = v - __bfloat162float(a);
+  const __nv_bfloat16 b = __float2bfloat16_rn(r1);
+  const float r2 = r1 - __bfloat162float(b);
+  const __nv_bfloat16 c = __float2bfloat16_rn(r2);
+  h[0] = __bfloat16_as_ushort(a);
+  h[1] = __bfloat16_as_ushort(b);
+  h[2] = __bfloat16_as_ushort(c);
+}
+
+// P^T and dS^T for H query columns of one key row of the fused backward, whose S^T and dP^T already hold
+// S^T - M/qk_scale and dP^T - delta (folded into the MMAs): P = exp2(S'^T * qk_scale), dS = P * dP'^T.
+// MASK keeps only columns c_lo <= c < c_hi.
+template <int H, bool MASK>
+__device__ __forceinline__ void pds_row_folded(const uint32_t* s, const uint32_t* dp, uint32_t* pt, uint32_t* dst,
+                                               uint64_t scale2, int c_lo, int c_hi) {
+#pragma unroll
+  for (int c = 0; c < H; c += 2) {
+    const uint64_t x = fmul2(f2(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), scale2);
+    float2 e = (((c / 2) & 7) < kDkvEmuPairs) ? exp2_pair<true>(x) : exp2_pair<false>(x);
+    if (MASK) {
+      e.x = (c >= c_lo && c < c_hi) ? e.x : 0.f;
+      e.y = (c + 1 >= c_lo && c + 1 < c_hi) ? e.y : 0.f;
+    }
+    pt[c / 2] = pack_half2(e.x, e.y);
+    const float2 v = f2_unpack(fmul2(f2(e.x, e.y), f2(__uint_as_float(dp[c]), __uint_as_float(dp[c + 1]))));
+    dst[c / 2] = pack_half2(v.x, v.y);
+  }
+}
+
+// TMA producer of the split dK/dV kernel (whole warp; lane 0 issues the copies): the CTA's key and value
+// tiles once, then per query block its Q and dO blocks (ring slot c % NS) and, staged by all lanes into
+// the slot's 16 * BQ bytes, the bf16 parts of -M/qk_scale and -delta of its BQ queries (the B operand of
+// the folded K step of the S^T / dP^T MMAs, as in the fused kernel).
 template <int D, int BQ, int NS>
 __device__ __forceinline__ void dkdv_producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const CUtensorMap* tm_v,
                                               const CUtensorMap* tm_do, const BwdArgs& args, uint32_t sK, uint32_t sV,
-                                              uint32_t sQ, uint32_t sDO, float* md, uint64_t* bar_kv,
+                                              uint32_t sQ, uint32_t sDO, uint8_t* md, uint64_t* bar_kv,
                                               uint64_t* bar_q_full, uint64_t* bar_md_full, uint64_t* bar_q_empty,
                                               int bh, int zi, int hi, int k0, int lo, int n, const CtaAbort& ab) {
   using G = Geo<D>;
@@ -997,13 +1035,18 @@ __device__ __forceinline__ void dkdv_producer(const CUtensorMap* tm_q, const CUt
         tma_load_4d(sDO + st * T_Q + ch * G::chunk(BQ), tm_do, ch * G::CW, qr, hi, zi, &bar_q_full[st]);
       }
     }
-    float* slot = md + st * 2 * BQ;
+    uint8_t* slot = md + st * BQ * 16;
+    const float inv_scale = 1.f / fold_scale(args.qk_scale);
 #pragma unroll
     for (int j = lane; j < BQ; j += 32) {
       const int q = qr + j;
-      slot[j] = q < N ? -mrow[q] : 0.f;
-      slot[BQ + j] = q < N ? -drow[q] : 0.f;
+      uint32_t hm[3], hd[3];
+      split_bf16x3(q < N ? -mrow[q] * inv_scale : 0.f, hm);
+      split_bf16x3(q < N ? -drow[q] : 0.f, hd);
+      *reinterpret_cast<uint4*>(slot + j * 16) =
+          make_uint4(hm[0] | (hm[1] << 16), hm[2] | (hd[0] << 16), hd[1] | (hd[2] << 16), 0u);
     }
+    fence_proxy_async_smem();  // read by the S^T / dP^T MMAs through the async proxy
     mbar_arrive(&bar_md_full[st]);
   }
   if (lane == 0) {
@@ -1365,8 +1408,11 @@ struct DkvSplitCfg {
   static constexpr int OFF_V = T_KEY;
   static constexpr int OFF_Q = 2 * T_KEY;            // NS query blocks
   static constexpr int OFF_DO = OFF_Q + NS * T_Q;    // NS dO blocks
-  static constexpr int OFF_MD = OFF_DO + NS * T_Q;   // NS x (BQ -M | BQ -delta) fp32
-  static constexpr int OFF_BAR = OFF_MD + NS * 2 * BQ * 4;
+  static constexpr int MD_SLOT = BQ * 16;            // bf16 parts of -M/qk_scale and -delta per query
+  static constexpr int OFF_MD = OFF_DO + NS * T_Q;   // NS x MD_SLOT
+  static constexpr int ONES_TILE = 128 * 32;         // constant A of the folded K step
+  static constexpr int OFF_ONES = OFF_MD + NS * MD_SLOT;  // 2 x ONES_TILE
+  static constexpr int OFF_BAR = OFF_ONES + 2 * ONES_TILE;
   // kv_full, q_full[NS], md_full[NS], q_empty[NS], s_full, s_free, p_full, acc_free, acc_done, fin[2]
   static constexpr int NBARS = 1 + 3 * NS + 7;
   static constexpr int OFF_MISC = OFF_BAR + NBARS * 8;
@@ -1376,8 +1422,10 @@ struct DkvSplitCfg {
   static constexpr uint32_t T_DV = 3 * BQ, T_DK = 3 * BQ + D;
   static_assert(3 * BQ + 2 * D <= 512, "TMEM budget");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+  static_assert(OFF_MD % 128 == 0 && OFF_ONES % 128 == 0, "alignment");
   static constexpr uint32_t IDESC_S = idesc_f16_f32(128, BQ, false);
   static constexpr uint32_t IDESC_ACC = idesc_f16_f32(128, D, true);
+  static constexpr uint32_t IDESC_MD = idesc_f16_f32(128, BQ, false) | (1u << 7) | (1u << 10);  // bf16 A, B
 };
 
 template <int D, bool CAUSAL, int BQ>
@@ -1403,7 +1451,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bar_acc_free = bar_s_full + 3;
   uint64_t* bar_acc_done = bar_s_full + 4;
   uint64_t* bar_fin = bar_s_full + 5;           // [2]: one per issuer warp
-  float* md = reinterpret_cast<float*>(smem + C::OFF_MD);  // per ring slot: -M [BQ] | -delta [BQ]
+  uint8_t* md = smem + C::OFF_MD;  // per ring slot: [BQ queries x 16 B] bf16 parts of -M/qk_scale, -delta
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
   const CtaAbort ab{abort_flag, args.status, args.wait_limit_ns};
@@ -1448,6 +1496,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tm_v);
     tma_prefetch_desc(&tm_do);
   }
+  // Constant A operands of the folded -M / -delta K step (as in the fused kernel; bf16 1.0 = 0x3F80).
+  for (int idx = threadIdx.x; idx < 2 * C::ONES_TILE / 16; idx += blockDim.x) {
+    const int t = idx / (C::ONES_TILE / 16), byte = (idx % (C::ONES_TILE / 16)) * 16;
+    const uint4 row = t == 0 ? make_uint4(0x3F803F80u, 0x00003F80u, 0u, 0u) : make_uint4(0u, 0x3F800000u, 0x3F803F80u, 0u);
+    *reinterpret_cast<uint4*>(smem + C::OFF_ONES + t * C::ONES_TILE + byte) =
+        (byte % 256) < 128 ? row : make_uint4(0u, 0u, 0u, 0u);
+  }
+  fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -1467,21 +1523,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t dV = smem_desc(sV, 16, 8 * G::SWB, G::LAYOUT);
       const uint64_t dQ = smem_desc(sQ, 16, 8 * G::SWB, G::LAYOUT);
       const uint64_t dDO = smem_desc(sDO, 16, 8 * G::SWB, G::LAYOUT);
+      const uint64_t dOnesM = smem_desc(base_u32 + C::OFF_ONES, 128, 256, 0u);
+      const uint64_t dOnesD = smem_desc(base_u32 + C::OFF_ONES + C::ONES_TILE, 128, 256, 0u);
+      const uint64_t dMD = smem_desc(base_u32 + C::OFF_MD, 0, 128, 0u);
+      // S'^T = S^T - M/qk_scale, dP'^T = dP^T - delta: the K = D steps, then one folded bf16 K step each.
       auto issue_s = [&](int c) {
         const uint64_t so = uint64_t(((c % C::NS) * C::T_Q) >> 4);
+        const uint64_t mo = uint64_t(((c % C::NS) * C::MD_SLOT) >> 4);
         mma_kmajor<D, G::chunk(128), G::chunk(BQ)>(tmem + C::T_ST, dK, dQ + so, idesc_s);
+        mma_f16_ss_elect(tmem + C::T_ST, dOnesM, dMD + mo, C::IDESC_MD, 1u);
         mma_kmajor<D, G::chunk(128), G::chunk(BQ)>(tmem + C::T_DPT, dV, dDO + so, C::IDESC_S);
+        mma_f16_ss_elect(tmem + C::T_DPT, dOnesD, dMD + mo, C::IDESC_MD, 1u);
         mma_commit_elect(bar_s_full);
         mma_commit_elect(&bar_q_empty[c % C::NS]);
       };
-      bool ok = n > 0 && warp_wait(bar_kv, 0, ab) && warp_wait(&bar_q_full[0], 0, ab);
+      bool ok = n > 0 && warp_wait(bar_kv, 0, ab) && warp_wait(&bar_q_full[0], 0, ab) &&
+                warp_wait(&bar_md_full[0], 0, ab);
       if (ok) {
         tc_fence_after();
         issue_s(0);
       }
       for (int c = 0; ok && c + 1 < n; ++c) {
         const int b = c + 1;
-        if (!warp_wait(bar_s_free, c & 1, ab) || !warp_wait(&bar_q_full[b % C::NS], (b / C::NS) & 1, ab)) break;
+        if (!warp_wait(bar_s_free, c & 1, ab) || !warp_wait(&bar_q_full[b % C::NS], (b / C::NS) & 1, ab) ||
+            !warp_wait(&bar_md_full[b % C::NS], (b / C::NS) & 1, ab))
+          break;
         tc_fence_after();
         issue_s(b);
       }
@@ -1512,10 +1578,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = threadIdx.x % 128;   // key row within the tile = TMEM lane
     const int key = k0 + r;
     const uint32_t tl = tmem + (uint32_t((warp % 4) * 32) << 16);
-    const uint64_t scale2 = f2(args.qk_scale, args.qk_scale);
+    const uint64_t scale2 = f2(fold_scale(args.qk_scale), fold_scale(args.qk_scale));
     bool ok = true;
     for (int c = 0; c < n; ++c) {
-      const int st = c % C::NS;
       if (!warp_wait(bar_s_full, c & 1, ab)) { ok = false; break; }
       tc_fence_after();
       uint32_t s[H], dp[H];
@@ -1526,17 +1591,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       reg_fence<H>(dp);
       tc_fence_before();
       mbar_arrive(bar_s_free);  // the tensor core may now write S^T/dP^T of the next block
-      if (!warp_wait(&bar_md_full[st], (c / C::NS) & 1, ab)) { ok = false; break; }
-      const float* mq = md + st * 2 * BQ + w * H;
       const int q0 = (lo + c) * BQ + w * H;  // first query column of this warpgroup's half
       const bool masked = (q0 + H > N) || (k0 + 128 > N) || (CAUSAL && q0 < k0 + 127);
       const int c_lo = CAUSAL ? max(0, key - q0) : 0;  // valid query columns: c_lo <= c < c_hi
       const int c_hi = key < N ? N - q0 : 0;
       uint32_t pt[H / 2], dst[H / 2];
       if (masked)
-        pds_row<H, true>(s, dp, mq, mq + BQ, pt, dst, scale2, c_lo, c_hi);
+        pds_row_folded<H, true>(s, dp, pt, dst, scale2, c_lo, c_hi);
       else
-        pds_row<H, false>(s, dp, mq, mq + BQ, pt, dst, scale2, c_lo, c_hi);
+        pds_row_folded<H, false>(s, dp, pt, dst, scale2, c_lo, c_hi);
       if (c > 0) {  // the dV/dK MMAs of the previous block have read P^T/dS^T
         if (!warp_wait(bar_acc_free, (c - 1) & 1, ab)) { ok = false; break; }
         tc_fence_after();
@@ -1708,38 +1771,6 @@ struct FusedCfg {
   static constexpr uint32_t IDESC_MD = idesc_f16_f32(128, BQ, false) | (1u << 7) | (1u << 10);  // bf16 A, B
 };
 
-// v as the sum of three bf16 values (exact: each step leaves at most 8 fewer significant bits).
-__device__ __forceinline__ void split_bf16x3(float v, uint32_t* h) {
-  const __nv_bfloat16 a = __float2bfloat16_rn(v);
-  const float r1 = v - __bfloat162float(a);
-  const __nv_bfloat16 b = __float2bfloat16_rn(r1);
-  const float r2 = r1 - __bfloat162float(b);
-  const __nv_bfloat16 c = __float2bfloat16_rn(r2);
-  h[0] = __bfloat16_as_ushort(a);
-  h[1] = __bfloat16_as_ushort(b);
-  h[2] = __bfloat16_as_ushort(c);
-}
-
-// P^T and dS^T for H query columns of one key row of the fused backward, whose S^T and dP^T already hold
-// S^T - M/qk_scale and dP^T - delta (folded into the MMAs): P = exp2(S'^T * qk_scale), dS = P * dP'^T.
-// MASK keeps only columns c_lo <= c < c_hi.
-template <int H, bool MASK>
-__device__ __forceinline__ void pds_row_folded(const uint32_t* s, const uint32_t* dp, uint32_t* pt, uint32_t* dst,
-                                               uint64_t scale2, int c_lo, int c_hi) {
-#pragma unroll
-  for (int c = 0; c < H; c += 2) {
-    const uint64_t x = fmul2(f2(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), scale2);
-    float2 e = (((c / 2) & 7) < kDkvEmuPairs) ? exp2_pair<true>(x) : exp2_pair<false>(x);
-    if (MASK) {
-      e.x = (c >= c_lo && c < c_hi) ? e.x : 0.f;
-      e.y = (c + 1 >= c_lo && c + 1 < c_hi) ? e.y : 0.f;
-    }
-    pt[c / 2] = pack_half2(e.x, e.y);
-    const float2 v = f2_unpack(fmul2(f2(e.x, e.y), f2(__uint_as_float(dp[c]), __uint_as_float(dp[c + 1]))));
-    dst[c / 2] = pack_half2(v.x, v.y);
-  }
-}
-
 // Add the warp's part of a block's dQ partial (32 query rows x D/2 fp32 columns, in registers) into the
 // fp32 workspace at (col, row) through the warp's staging area.
 template <int D>
@@ -1902,7 +1933,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++kv_issued;
         const float* mrow = args.m + int64_t(bh) * N;
         const float* drow = args.delta + int64_t(bh) * N;
-        const float inv_scale = 1.f / args.qk_scale;  // qk_scale > 0 here (the host takes sm_scale = 0 elsewhere)
+        const float inv_scale = 1.f / fold_scale(args.qk_scale);
         for (int c = 0; c < n; ++c, ++g) {
           const int st = g % NS;
           if (g >= NS && !warp_wait(&bar_q_empty[st], ((g / NS) - 1) & 1, ab)) { ok = false; break; }
@@ -2057,7 +2088,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t stg = base_u32 + C::OFF_STG + warp * C::STG;
     // This thread's row of dS^T: key r, queries [64 w, 64 w + 64) = one 128-byte row of chunk w.
     const uint32_t ds_row = sDS + w * C::DS_CHUNK + r * 128;
-    const uint64_t scale2 = f2(args.qk_scale, args.qk_scale);
+    const uint64_t scale2 = f2(fold_scale(args.qk_scale), fold_scale(args.qk_scale));
     const CUtensorMap* tm_out = w ? &tm_dk : &tm_dv;
     const float mul = w ? args.sm_scale : 1.f;
     int g = 0, it = 0;

@@ -3,7 +3,6 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
-#include <math.h>
 #include <stdint.h>
 
 #include <atomic>
@@ -321,22 +320,6 @@ extern "C" int tattn_bwd_fused(const void* q, const void* k, const void* v, cons
   if (dtype != TATTN_F16 || D > 64) return TATTN_ERR_UNSUPPORTED;
   if (int64_t(Z) * H * N == 0) return TATTN_OK;
   if (!q || !k || !v || !o || !dout || !dq || !dk || !dv || !m || !delta || !dq_acc) return TATTN_ERR_INVALID_ARGUMENT;
-  if (!(fabsf(sm_scale) > 1e-30f)) {
-    // The fused kernel folds -M / (|sm_scale| log2 e) into its S^T MMA, which needs a scale it can
-    // invert; sm_scale = 0 (or a subnormal one) runs the three-kernel backward on the same buffers.
-    const int64_t pre[8] = {strides[12], strides[13], strides[14], strides[15],
-                            strides[16], strides[17], strides[18], strides[19]};
-    const int64_t qkvdo[16] = {strides[0], strides[1], strides[2],  strides[3],  strides[4],  strides[5],
-                               strides[6], strides[7], strides[8],  strides[9],  strides[10], strides[11],
-                               strides[16], strides[17], strides[18], strides[19]};
-    int rc = tattn_bwd_preprocess(o, dout, delta, pre, Z, H, N, D, dtype, stream);
-    if (rc != TATTN_OK) return rc;
-    rc = bwd_common(false, q, k, v, dout, nullptr, dk, dv, m, delta, qkvdo, Z, H, N, D, dtype, causal, sm_scale, 0,
-                    stream);
-    if (rc != TATTN_OK) return rc;
-    return bwd_common(true, q, k, v, dout, dq, nullptr, nullptr, m, delta, qkvdo, Z, H, N, D, dtype, causal,
-                      sm_scale, 0, stream);
-  }
   DeviceState* st;
   int rc = device_setup(&st);
   if (rc != TATTN_OK) return rc;
