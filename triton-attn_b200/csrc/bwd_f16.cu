@@ -1001,10 +1001,11 @@ __device__ __forceinline__ void pds_row_folded(const uint32_t* s, const uint32_t
 }
 
 // TMA producer of the split dK/dV kernel (whole warp; lane 0 issues the copies): the CTA's key and value
-// tiles once, then per query block its Q and dO blocks (ring slot c % NS) and, staged by all lanes into
-// the slot's 16 * BQ bytes, the bf16 parts of -M/qk_scale and -delta of its BQ queries (the B operand of
-// the folded K step of the S^T / dP^T MMAs, as in the fused kernel).
-template <int D, int BQ, int NS>
+// tiles once, then per query block its Q and dO blocks (ring slot c % NS) and, staged by all lanes, the
+// -M / -delta values of its BQ queries: FOLD, the bf16 parts of -M/qk_scale and -delta (16 bytes a query,
+// the B operand of the folded K step of the S^T / dP^T MMAs, as in the fused kernel); otherwise -M and
+// -delta as fp32 (BQ of each) for the compute warps to read.
+template <int D, int BQ, int NS, bool FOLD>
 __device__ __forceinline__ void dkdv_producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const CUtensorMap* tm_v,
                                               const CUtensorMap* tm_do, const BwdArgs& args, uint32_t sK, uint32_t sV,
                                               uint32_t sQ, uint32_t sDO, uint8_t* md, uint64_t* bar_kv,
@@ -1035,18 +1036,28 @@ __device__ __forceinline__ void dkdv_producer(const CUtensorMap* tm_q, const CUt
         tma_load_4d(sDO + st * T_Q + ch * G::chunk(BQ), tm_do, ch * G::CW, qr, hi, zi, &bar_q_full[st]);
       }
     }
-    uint8_t* slot = md + st * BQ * 16;
-    const float inv_scale = 1.f / fold_scale(args.qk_scale);
+    if constexpr (FOLD) {
+      uint8_t* slot = md + st * BQ * 16;
+      const float inv_scale = 1.f / fold_scale(args.qk_scale);
 #pragma unroll
-    for (int j = lane; j < BQ; j += 32) {
-      const int q = qr + j;
-      uint32_t hm[3], hd[3];
-      split_bf16x3(q < N ? -mrow[q] * inv_scale : 0.f, hm);
-      split_bf16x3(q < N ? -drow[q] : 0.f, hd);
-      *reinterpret_cast<uint4*>(slot + j * 16) =
-          make_uint4(hm[0] | (hm[1] << 16), hm[2] | (hd[0] << 16), hd[1] | (hd[2] << 16), 0u);
+      for (int j = lane; j < BQ; j += 32) {
+        const int q = qr + j;
+        uint32_t hm[3], hd[3];
+        split_bf16x3(q < N ? -mrow[q] * inv_scale : 0.f, hm);
+        split_bf16x3(q < N ? -drow[q] : 0.f, hd);
+        *reinterpret_cast<uint4*>(slot + j * 16) =
+            make_uint4(hm[0] | (hm[1] << 16), hm[2] | (hd[0] << 16), hd[1] | (hd[2] << 16), 0u);
+      }
+      fence_proxy_async_smem();  // read by the S^T / dP^T MMAs through the async proxy
+    } else {
+      float* slot = reinterpret_cast<float*>(md) + st * 2 * BQ;
+#pragma unroll
+      for (int j = lane; j < BQ; j += 32) {
+        const int q = qr + j;
+        slot[j] = q < N ? -mrow[q] : 0.f;
+        slot[BQ + j] = q < N ? -drow[q] : 0.f;
+      }
     }
-    fence_proxy_async_smem();  // read by the S^T / dP^T MMAs through the async proxy
     mbar_arrive(&bar_md_full[st]);
   }
   if (lane == 0) {
@@ -1408,9 +1419,14 @@ struct DkvSplitCfg {
   static constexpr int OFF_V = T_KEY;
   static constexpr int OFF_Q = 2 * T_KEY;            // NS query blocks
   static constexpr int OFF_DO = OFF_Q + NS * T_Q;    // NS dO blocks
-  static constexpr int MD_SLOT = BQ * 16;            // bf16 parts of -M/qk_scale and -delta per query
+  // -M and -delta reach S^T and dP^T through one more MMA K step when D <= 64 (see the fused kernel). At
+  // D = 128 every block already carries twice the MMA work per exponential and the extra step costs
+  // more than the shared-memory loads it saves (measured: -10 % non-causal), so there the compute warps
+  // read fp32 -M / -delta from shared memory.
+  static constexpr bool FOLD = D <= 64;
+  static constexpr int MD_SLOT = FOLD ? BQ * 16 : 2 * BQ * 4;
   static constexpr int OFF_MD = OFF_DO + NS * T_Q;   // NS x MD_SLOT
-  static constexpr int ONES_TILE = 128 * 32;         // constant A of the folded K step
+  static constexpr int ONES_TILE = FOLD ? 128 * 32 : 0;  // constant A of the folded K step
   static constexpr int OFF_ONES = OFF_MD + NS * MD_SLOT;  // 2 x ONES_TILE
   static constexpr int OFF_BAR = OFF_ONES + 2 * ONES_TILE;
   // kv_full, q_full[NS], md_full[NS], q_empty[NS], s_full, s_free, p_full, acc_free, acc_done, fin[2]
@@ -1497,7 +1513,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tm_do);
   }
   // Constant A operands of the folded -M / -delta K step (as in the fused kernel; bf16 1.0 = 0x3F80).
-  for (int idx = threadIdx.x; idx < 2 * C::ONES_TILE / 16; idx += blockDim.x) {
+  for (int idx = threadIdx.x; C::FOLD && idx < 2 * C::ONES_TILE / 16; idx += blockDim.x) {
     const int t = idx / (C::ONES_TILE / 16), byte = (idx % (C::ONES_TILE / 16)) * 16;
     const uint4 row = t == 0 ? make_uint4(0x3F803F80u, 0x00003F80u, 0u, 0u) : make_uint4(0u, 0x3F800000u, 0x3F803F80u, 0u);
     *reinterpret_cast<uint4*>(smem + C::OFF_ONES + t * C::ONES_TILE + byte) =
@@ -1514,7 +1530,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp >= kTmaWarp) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
     if (warp == kTmaWarp) {
-      dkdv_producer<D, BQ, C::NS>(&tm_q, &tm_k, &tm_v, &tm_do, args, sK, sV, sQ, sDO, md, bar_kv, bar_q_full,
+      dkdv_producer<D, BQ, C::NS, C::FOLD>(&tm_q, &tm_k, &tm_v, &tm_do, args, sK, sV, sQ, sDO, md, bar_kv, bar_q_full,
                                   bar_md_full, bar_q_empty, bh, zi, hi, k0, lo, n, ab);
     } else if (warp == kMmaSWarp) {
       // -------------------------------------------------------------- S^T/dP^T issuer
@@ -1531,14 +1547,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t so = uint64_t(((c % C::NS) * C::T_Q) >> 4);
         const uint64_t mo = uint64_t(((c % C::NS) * C::MD_SLOT) >> 4);
         mma_kmajor<D, G::chunk(128), G::chunk(BQ)>(tmem + C::T_ST, dK, dQ + so, idesc_s);
-        mma_f16_ss_elect(tmem + C::T_ST, dOnesM, dMD + mo, C::IDESC_MD, 1u);
+        if constexpr (C::FOLD) mma_f16_ss_elect(tmem + C::T_ST, dOnesM, dMD + mo, C::IDESC_MD, 1u);
         mma_kmajor<D, G::chunk(128), G::chunk(BQ)>(tmem + C::T_DPT, dV, dDO + so, C::IDESC_S);
-        mma_f16_ss_elect(tmem + C::T_DPT, dOnesD, dMD + mo, C::IDESC_MD, 1u);
+        if constexpr (C::FOLD) mma_f16_ss_elect(tmem + C::T_DPT, dOnesD, dMD + mo, C::IDESC_MD, 1u);
         mma_commit_elect(bar_s_full);
         mma_commit_elect(&bar_q_empty[c % C::NS]);
       };
       bool ok = n > 0 && warp_wait(bar_kv, 0, ab) && warp_wait(&bar_q_full[0], 0, ab) &&
-                warp_wait(&bar_md_full[0], 0, ab);
+                (!C::FOLD || warp_wait(&bar_md_full[0], 0, ab));
       if (ok) {
         tc_fence_after();
         issue_s(0);
@@ -1546,7 +1562,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; ok && c + 1 < n; ++c) {
         const int b = c + 1;
         if (!warp_wait(bar_s_free, c & 1, ab) || !warp_wait(&bar_q_full[b % C::NS], (b / C::NS) & 1, ab) ||
-            !warp_wait(&bar_md_full[b % C::NS], (b / C::NS) & 1, ab))
+            (C::FOLD && !warp_wait(&bar_md_full[b % C::NS], (b / C::NS) & 1, ab)))
           break;
         tc_fence_after();
         issue_s(b);
@@ -1578,9 +1594,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = threadIdx.x % 128;   // key row within the tile = TMEM lane
     const int key = k0 + r;
     const uint32_t tl = tmem + (uint32_t((warp % 4) * 32) << 16);
-    const uint64_t scale2 = f2(fold_scale(args.qk_scale), fold_scale(args.qk_scale));
+    const float sc = C::FOLD ? fold_scale(args.qk_scale) : args.qk_scale;
+    const uint64_t scale2 = f2(sc, sc);
     bool ok = true;
     for (int c = 0; c < n; ++c) {
+      const int st = c % C::NS;
       if (!warp_wait(bar_s_full, c & 1, ab)) { ok = false; break; }
       tc_fence_after();
       uint32_t s[H], dp[H];
@@ -1591,15 +1609,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       reg_fence<H>(dp);
       tc_fence_before();
       mbar_arrive(bar_s_free);  // the tensor core may now write S^T/dP^T of the next block
+      const float* mq = reinterpret_cast<const float*>(md) + st * 2 * BQ + w * H;  // unfolded -M | -delta
+      if (!C::FOLD && !warp_wait(&bar_md_full[st], (c / C::NS) & 1, ab)) { ok = false; break; }
       const int q0 = (lo + c) * BQ + w * H;  // first query column of this warpgroup's half
       const bool masked = (q0 + H > N) || (k0 + 128 > N) || (CAUSAL && q0 < k0 + 127);
       const int c_lo = CAUSAL ? max(0, key - q0) : 0;  // valid query columns: c_lo <= c < c_hi
       const int c_hi = key < N ? N - q0 : 0;
       uint32_t pt[H / 2], dst[H / 2];
-      if (masked)
-        pds_row_folded<H, true>(s, dp, pt, dst, scale2, c_lo, c_hi);
-      else
-        pds_row_folded<H, false>(s, dp, pt, dst, scale2, c_lo, c_hi);
+      if constexpr (C::FOLD) {
+        if (masked)
+          pds_row_folded<H, true>(s, dp, pt, dst, scale2, c_lo, c_hi);
+        else
+          pds_row_folded<H, false>(s, dp, pt, dst, scale2, c_lo, c_hi);
+      } else {
+        if (masked)
+          pds_row<H, true>(s, dp, mq, mq + BQ, pt, dst, scale2, c_lo, c_hi);
+        else
+          pds_row<H, false>(s, dp, mq, mq + BQ, pt, dst, scale2, c_lo, c_hi);
+      }
       if (c > 0) {  // the dV/dK MMAs of the previous block have read P^T/dS^T
         if (!warp_wait(bar_acc_free, (c - 1) & 1, ab)) { ok = false; break; }
         tc_fence_after();
