@@ -774,7 +774,9 @@ def run_variants(args) -> None:
                 for i, cfg in enumerate(api.TILE_CONFIGS["fwd"]) if api.tile_supported(cfg, "fwd", d)]
         runs += [("bwd_split", i + 1, cfg, lambda cfg=cfg: api._backward(q, k, v, o, m, do, causal, sc, config=cfg),
                   2.5 * f) for i, cfg in enumerate(api.TILE_CONFIGS["bwd"]) if api.tile_supported(cfg, "bwd", d)]
-        runs.append(("bwd_fused", 0, {}, lambda: api._backward(q, k, v, o, m, do, causal, sc), 2.5 * f))
+        # the API's own backward: the fused kernel for D <= 64, the split default above it
+        runs.append(("bwd_fused" if d <= 64 else "bwd_api_split", 0, {},
+                     lambda: api._backward(q, k, v, o, m, do, causal, sc), 2.5 * f))
         for kind, idx, cfg, fn, fl in runs:
             for _ in range(args.warmup):
                 fn()
@@ -784,7 +786,7 @@ def run_variants(args) -> None:
             default = _lib.load().tattn_tile_default(api._KIND["fwd" if kind == "fwd" else "bwd"], d, int(causal), 0)
             print(json.dumps({"variants": name, "kind": kind, "tile_cfg": idx, **cfg, "ms": round(ms, 4),
                               "tflops": round(fl / (ms * 1e-3) / 1e12, 1),
-                              "default": kind == "bwd_fused" or idx == default}),
+                              "default": kind in ("bwd_fused", "bwd_api_split") or idx == default}),
                   flush=True)  # fmt: skip
         del q, k, v, do, o, m
         torch.cuda.empty_cache()
