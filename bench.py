@@ -308,12 +308,11 @@ def _isolated_kernel_times(q, k, v, do, causal, scale, iters: int) -> dict:
         "dq": lambda: lib.tattn_bwd_dq(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), dq.data_ptr(),
                                        m.data_ptr(), delta.data_ptr(), st, z, h, n, d, 0, ci, scale, 0, stream),
     }  # fmt: skip
-    if d <= 64:
-        ws = torch.empty((z, h, n, d), device=q.device, dtype=torch.float32)
-        st5 = _lib.strides_array(q.stride(), k.stride(), v.stride(), o.stride(), do.stride())
-        calls["bwd_fused"] = lambda: lib.tattn_bwd_fused(
-            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), dq.data_ptr(), dk.data_ptr(),
-            dv.data_ptr(), m.data_ptr(), delta.data_ptr(), ws.data_ptr(), st5, z, h, n, d, 0, ci, scale, stream)
+    ws = torch.empty((z, h, n, d), device=q.device, dtype=torch.float32)
+    st5 = _lib.strides_array(q.stride(), k.stride(), v.stride(), o.stride(), do.stride())
+    calls["bwd_fused"] = lambda: lib.tattn_bwd_fused(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), dq.data_ptr(), dk.data_ptr(),
+        dv.data_ptr(), m.data_ptr(), delta.data_ptr(), ws.data_ptr(), st5, z, h, n, d, 0, ci, scale, stream)
     out = {}
     for name, fn in calls.items():
         for _ in range(3):
@@ -774,19 +773,19 @@ def run_variants(args) -> None:
                 for i, cfg in enumerate(api.TILE_CONFIGS["fwd"]) if api.tile_supported(cfg, "fwd", d)]
         runs += [("bwd_split", i + 1, cfg, lambda cfg=cfg: api._backward(q, k, v, o, m, do, causal, sc, config=cfg),
                   2.5 * f) for i, cfg in enumerate(api.TILE_CONFIGS["bwd"]) if api.tile_supported(cfg, "bwd", d)]
-        # the API's own backward: the fused kernel for D <= 64, the split default above it
-        runs.append(("bwd_fused" if d <= 64 else "bwd_api_split", 0, {},
+        # the API's own fp16 backward: the fused kernel
+        runs.append(("bwd_fused", 0, {},
                      lambda: api._backward(q, k, v, o, m, do, causal, sc), 2.5 * f))
         for kind, idx, cfg, fn, fl in runs:
             for _ in range(args.warmup):
                 fn()
             ms = timer(fn, args.steps) / args.steps
             # tile_cfg 0 of tattn_fwd / the split backward resolves to this variant; the API's fp16 backward
-            # for D <= 64 is the fused kernel
+            # is the fused kernel
             default = _lib.load().tattn_tile_default(api._KIND["fwd" if kind == "fwd" else "bwd"], d, int(causal), 0)
             print(json.dumps({"variants": name, "kind": kind, "tile_cfg": idx, **cfg, "ms": round(ms, 4),
                               "tflops": round(fl / (ms * 1e-3) / 1e12, 1),
-                              "default": kind in ("bwd_fused", "bwd_api_split") or idx == default}),
+                              "default": kind == "bwd_fused" or idx == default}),
                   flush=True)  # fmt: skip
         del q, k, v, do, o, m
         torch.cuda.empty_cache()

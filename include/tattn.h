@@ -94,8 +94,9 @@ TATTN_API int tattn_bwd_dq(const void* q, const void* k, const void* v, const vo
  * aligned; zeroed here), then scaled into dq; the order of those additions varies from run to run, so
  * dq is not bitwise reproducible (dk and dv are). strides: 20 int64 = q, k, v, o, dout each
  * (z, h, n, d); dq, dk, dv dense [Z, H, N, D].
- * fp16 with D <= 64 only (causal or not): other requests return TATTN_ERR_UNSUPPORTED (use the three
- * calls). */
+ * fp16 only (every supported D, causal or not; at D = 128 the query blocks are 64 rows and each block's
+ * dQ part is computed transposed, dQ^T = K^T dS^T, to fit tensor memory): fp32 requests return
+ * TATTN_ERR_UNSUPPORTED (use the three calls). */
 TATTN_API int tattn_bwd_fused(const void* q, const void* k, const void* v, const void* o, const void* dout,
                     void* dq, void* dk, void* dv, const float* m, float* delta, float* dq_acc,
                     const int64_t* strides, int Z, int H, int N, int D, int dtype, int causal, float sm_scale,

@@ -1752,16 +1752,20 @@ cudaError_t dkdv_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtens
 template <int D>
 struct FusedCfg {
   using G = Geo<D>;
-  static_assert(D <= 64, "fused backward: TMEM holds S^T, dP^T, P^T, dV, dK and the dQ partial");
-  static constexpr int BQ = 128, H = 64;
-  static constexpr int NS = 3;                            // Q/dO ring stages
+  // D = 128: 64-query blocks, and the dQ part computed transposed (dQ^T = K^T dS^T: 128 head-dim lanes x
+  // 64 query columns), so that S^T, dP^T, P^T, dV, dK and the dQ part still fit TMEM's 512 columns
+  // (64 + 64 + 32 + 128 + 128 + 64 = 480); with 128-query blocks and dQ = dS K they would need 704.
+  static constexpr bool DQT = D == 128;
+  static constexpr int BQ = DQT ? 64 : 128, H = BQ / 2;  // query rows per block, columns per warpgroup
+  static constexpr int NS = DQT ? 2 : 3;                  // Q/dO ring stages (shared memory)
   static constexpr int T_KEY = G::tile(128);
   static constexpr int T_Q = G::tile(BQ);
-  static constexpr int T_DS = Geo<128>::tile(128);        // dS^T [128 keys, 128 queries] fp16
+  static constexpr int T_DS = 128 * BQ * 2;               // dS^T [128 keys, BQ queries] fp16
   static constexpr int DS_CHUNK = Geo<128>::chunk(128);   // 64 queries of every key row
-  static constexpr int HW = D / 2;                        // output columns per warpgroup
+  static constexpr int HW = D / 2;                        // dK/dV output columns per warpgroup
+  static constexpr int QW = DQT ? 32 : D / 2;             // dQ-part columns per warpgroup (queries if DQT)
   static constexpr int SWB_O = HW * 2;                    // dK/dV staging row bytes (fp16)
-  static constexpr int SWB_Q = HW * 4;                    // dQ staging row bytes (fp32)
+  static constexpr int SWB_Q = DQT ? 128 : HW * 4;        // dQ staging row bytes (fp32; 32 head dims if DQT)
   static constexpr int STG_ROW = SWB_O > SWB_Q ? SWB_O : SWB_Q;
   static constexpr int STG = 32 * STG_ROW < 1024 ? 1024 : 32 * STG_ROW;  // per-warp staging, both uses
   static constexpr int OFF_K = 0;                         // [2 buffers] key tiles
@@ -1787,14 +1791,19 @@ struct FusedCfg {
   static constexpr int OFF_MISC = OFF_BAR + NBARS * 8;
   static constexpr int SMEM_USED = OFF_MISC + 16;
   static constexpr int SMEM_BYTES = (SMEM_USED > 118784 ? SMEM_USED : 118784) + 1024;
-  static constexpr uint32_t T_ST = 0, T_DPT = 128, T_PT = 256, T_DV = 320, T_DK = 320 + D, T_DQ = 320 + 2 * D;
-  static_assert(T_DQ + D <= 512, "TMEM budget");
+  // TMEM columns: S^T [BQ], dP^T [BQ], P^T [BQ / 2, fp16 pairs], dV [D], dK [D], the dQ part [DQC].
+  static constexpr int DQC = DQT ? BQ : D;
+  static constexpr uint32_t T_ST = 0, T_DPT = BQ;
+  static constexpr uint32_t T_DV = DQT ? 128 : 320, T_DK = T_DV + D, T_DQ = T_DK + D;
+  static constexpr uint32_t T_PT = DQT ? T_DQ + DQC : 256;
+  static_assert(T_DQ + DQC <= 512 && T_PT + BQ / 2 <= 512 && (DQT || T_PT + BQ / 2 <= T_DV), "TMEM budget");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
   static_assert(OFF_DS % 1024 == 0 && OFF_STG % 1024 == 0 && OFF_MD % 128 == 0 && OFF_ONES % 128 == 0,
                 "alignment");
   static constexpr uint32_t IDESC_S = idesc_f16_f32(128, BQ, false);
   static constexpr uint32_t IDESC_ACC = idesc_f16_f32(128, D, true);     // A K-major, B MN-major
-  static constexpr uint32_t IDESC_DQ = idesc_f16_f32_amn(128, D, true);  // A (dS) and B (K) MN-major
+  // A and B MN-major: dQ = dS K (A = dS, B = K) or, DQT, dQ^T = K^T dS^T (A = K^T, B = dS^T).
+  static constexpr uint32_t IDESC_DQ = idesc_f16_f32_amn(128, DQC, true);
   static constexpr uint32_t IDESC_MD = idesc_f16_f32(128, BQ, false) | (1u << 7) | (1u << 10);  // bf16 A, B
 };
 
@@ -1815,6 +1824,26 @@ __device__ __forceinline__ void fused_dq_out(const uint32_t* o, uint32_t stg, co
   fence_proxy_async_smem();
   __syncwarp();
   if (lane == 0) {  // rows past N are clipped by the tensor map
+    tma_reduce_add_4d(tm, stg, col, row, hi, zi);
+    tma_store_commit();
+  }
+}
+
+// D = 128: the warp holds a transposed dQ part (lane = one of 32 head dims, o[j] = query j of 32), written
+// transposed into the staging tile (32 query rows x 32 head-dim fp32, 128-byte swizzle; for each query
+// the 32 lanes store one 128-byte row, so the stores are conflict-free), then added like fused_dq_out.
+__device__ __forceinline__ void fused_dqt_out(const uint32_t* o, uint32_t stg, const CUtensorMap* tm, int col,
+                                              int row, int hi, int zi, int lane) {
+  if (lane == 0) tma_store_wait_read_all();
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const uint32_t addr = stg + swizzle_offset<128>(uint32_t(j * 128 + lane * 4));
+    asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(o[j]) : "memory");
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
     tma_reduce_add_4d(tm, stg, col, row, hi, zi);
     tma_store_commit();
   }
@@ -2044,7 +2073,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t dDOmn = smem_desc(sDO, G::chunk(BQ), 8 * G::SWB, G::LAYOUT);
       const uint64_t dKmn = smem_desc(sK, G::chunk(128), 8 * G::SWB, G::LAYOUT);
       const uint64_t dDSk = smem_desc(sDS, 16, 1024, 2u);                // dS^T as K-major A (dK)
-      const uint64_t dDSmn = smem_desc(sDS, C::DS_CHUNK, 1024, 2u);      // dS as MN-major A (dQ)
+      const uint64_t dDSmn = smem_desc(sDS, C::DS_CHUNK, 1024, 2u);      // dS (A) or dS^T (B), MN-major (dQ)
       int g = 0, it = 0;
       bool ok = true;
       int2 seq = make_int2(int(blockIdx.x), 0);
@@ -2071,14 +2100,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < BQ / 16; ++kk)
             mma_f16_ss_elect(tmem + C::T_DK, dDSk + uint64_t(((kk / 4) * C::DS_CHUNK + (kk % 4) * 32) >> 4),
                              dQmn + so + uint64_t((kk * 16 * G::SWB) >> 4), C::IDESC_ACC, kk > 0 ? 1u : acc);
-          // dQ_part = dS K (A = dS, MN-major: 16 key rows of 128 bytes per K step; B = K, MN-major), once
-          // the compute warps hold the previous block's dQ part.
+          // dQ_part = dS K (A = dS, MN-major: 16 key rows of 128 bytes per K step; B = K, MN-major) or, D =
+          // 128, dQ_part^T = K^T dS^T (the same two tiles as A = K^T and B = dS^T), once the compute warps
+          // hold the previous block's dQ part.
           if (!warp_wait(bar_dq_read, g & 1, ab)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < 128 / 16; ++kk)
-            mma_f16_ss_elect(tmem + C::T_DQ, dDSmn + uint64_t((kk * 16 * 128) >> 4),
-                             dKmn + ko + uint64_t((kk * 16 * G::SWB) >> 4), C::IDESC_DQ, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < 128 / 16; ++kk) {
+            const uint64_t ds_k = dDSmn + uint64_t((kk * 16 * 128) >> 4);
+            const uint64_t k_k = dKmn + ko + uint64_t((kk * 16 * G::SWB) >> 4);
+            if constexpr (C::DQT)
+              mma_f16_ss_elect(tmem + C::T_DQ, k_k, ds_k, C::IDESC_DQ, kk > 0 ? 1u : 0u);
+            else
+              mma_f16_ss_elect(tmem + C::T_DQ, ds_k, k_k, C::IDESC_DQ, kk > 0 ? 1u : 0u);
+          }
           mma_commit_elect(bar_acc_free);
           mma_commit_elect(&bar_q_empty[g % NS]);
         }
@@ -2113,8 +2148,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q4 = warp % 4;           // TMEM lane quadrant: rows [32 q4, 32 q4 + 32)
     const uint32_t tl = tmem + (uint32_t(q4 * 32) << 16);
     const uint32_t stg = base_u32 + C::OFF_STG + warp * C::STG;
-    // This thread's row of dS^T: key r, queries [64 w, 64 w + 64) = one 128-byte row of chunk w.
-    const uint32_t ds_row = sDS + w * C::DS_CHUNK + r * 128;
+    // This thread's row of dS^T: key r, queries [H w, H w + H): one 128-byte row of chunk w (H = 64), or
+    // 16-byte units [4 w, 4 w + 4) of the single chunk's row r (H = 32).
+    const uint32_t ds_row = sDS + (C::DQT ? 0 : w * C::DS_CHUNK) + r * 128;
+    constexpr int DS_U = H / 8;                 // 16-byte units of dS^T a thread writes per block
+    const int ds_u0 = C::DQT ? 4 * w : 0;
     const uint64_t scale2 = f2(fold_scale(args.qk_scale), fold_scale(args.qk_scale));
     const CUtensorMap* tm_out = w ? &tm_dk : &tm_dv;
     const float mul = w ? args.sm_scale : 1.f;
@@ -2150,8 +2188,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tmem_store_cols<H / 2>(tl + C::T_PT + w * (H / 2), pt);
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const uint32_t addr = ds_row + uint32_t((u ^ (r & 7)) << 4);
+        for (int u = 0; u < DS_U; ++u) {
+          const uint32_t addr = ds_row + uint32_t(((ds_u0 + u) ^ (r & 7)) << 4);
           asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(dst[4 * u]), "r"(dst[4 * u + 1]),
                        "r"(dst[4 * u + 2]), "r"(dst[4 * u + 3]) : "memory");
         }
@@ -2162,13 +2200,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         // The previous block's dQ part (the last block of a tile leaves in the epilogue): into registers,
         // release the accumulator to this block's dQ MMAs, then add it into the workspace.
         if (c > 0) {
-          uint32_t oq[C::HW];
-          tmem_load_cols<C::HW>(tl + C::T_DQ + w * C::HW, oq);
+          uint32_t oq[C::QW];
+          tmem_load_cols<C::QW>(tl + C::T_DQ + w * C::QW, oq);
           tmem_wait_ld();
-          reg_fence<C::HW>(oq);
+          reg_fence<C::QW>(oq);
           tc_fence_before();
           mbar_arrive(bar_dq_read);
-          fused_dq_out<D>(oq, stg, &tm_dqacc, w * C::HW, (lo + c - 1) * BQ + 32 * q4, hi, zi, lane);
+          if constexpr (C::DQT)
+            fused_dqt_out(oq, stg, &tm_dqacc, 32 * q4, (lo + c - 1) * BQ + 32 * w, hi, zi, lane);
+          else
+            fused_dq_out<D>(oq, stg, &tm_dqacc, w * C::HW, (lo + c - 1) * BQ + 32 * q4, hi, zi, lane);
         } else {
           mbar_arrive(bar_dq_read);
         }
@@ -2176,23 +2217,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok || !warp_wait(bar_acc_done, it & 1, ab)) { ok = false; break; }
       // ---- epilogue: the last block's dQ part, then dV (warpgroup 0) or dK * sm_scale (warpgroup 1)
       tc_fence_after();
-      uint32_t o[D];
-      tmem_load_cols<D>(tl + (w ? C::T_DK : C::T_DV), o);
-      uint32_t oq[C::HW];
-      tmem_load_cols<C::HW>(tl + C::T_DQ + w * C::HW, oq);
+      // D = 128 reads dV / dK one half at a time (64 registers, not 128), releasing the accumulators after
+      // the second half.
+      constexpr int OR = C::DQT ? C::HW : D;  // accumulator columns held in registers at a time
+      uint32_t o[OR];
+      tmem_load_cols<OR>(tl + (w ? C::T_DK : C::T_DV), o);
+      uint32_t oq[C::QW];
+      tmem_load_cols<C::QW>(tl + C::T_DQ + w * C::QW, oq);
       tmem_wait_ld();
-      reg_fence<D>(o);
-      reg_fence<C::HW>(oq);
-      tc_fence_before();
-      mbar_arrive(bar_acc_read);  // the next tile's first MMAs may overwrite the accumulators
-      fused_dq_out<D>(oq, stg, &tm_dqacc, w * C::HW, (lo + n - 1) * BQ + 32 * q4, hi, zi, lane);
+      reg_fence<OR>(o);
+      reg_fence<C::QW>(oq);
+      if constexpr (!C::DQT) {
+        tc_fence_before();
+        mbar_arrive(bar_acc_read);  // the next tile's first MMAs may overwrite the accumulators
+        fused_dq_out<D>(oq, stg, &tm_dqacc, w * C::HW, (lo + n - 1) * BQ + 32 * q4, hi, zi, lane);
+      } else {
+        fused_dqt_out(oq, stg, &tm_dqacc, 32 * q4, (lo + n - 1) * BQ + 32 * w, hi, zi, lane);
+      }
 #pragma unroll
       for (int half = 0; half < 2; ++half) {  // columns [half * HW, half * HW + HW)
+        if constexpr (C::DQT) {
+          if (half == 1) {
+            tmem_load_cols<OR>(tl + (w ? C::T_DK : C::T_DV) + C::HW, o);
+            tmem_wait_ld();
+            reg_fence<OR>(o);
+            tc_fence_before();
+            mbar_arrive(bar_acc_read);
+          }
+        }
         if (lane == 0) tma_store_wait_read_all();  // this warp's previous store has left the staging area
         __syncwarp();
 #pragma unroll
         for (int u = 0; u < C::SWB_O / 16; ++u) {
-          const int cc = half * C::HW + u * 8;
+          const int cc = (C::DQT ? 0 : half * C::HW) + u * 8;
           const uint32_t addr = stg + swizzle_offset<C::SWB_O>(uint32_t(lane * C::SWB_O + u * 16));
           const uint32_t h0 = pack_half2(__uint_as_float(o[cc + 0]) * mul, __uint_as_float(o[cc + 1]) * mul);
           const uint32_t h1 = pack_half2(__uint_as_float(o[cc + 2]) * mul, __uint_as_float(o[cc + 3]) * mul);
@@ -2317,6 +2374,9 @@ cudaError_t launch_bwd_dkdv_f16(int D, bool causal, int variant, const CUtensorM
   return split_dispatch<false>(D, causal, variant, tq, tk, tv, tdo, tdk, tdv, a, s);
 }
 
+static_assert(FusedCfg<64>::BQ == bwd_fused_query_rows(64) && FusedCfg<128>::BQ == bwd_fused_query_rows(128),
+              "fused backward query blocks");
+
 cudaError_t launch_bwd_fused_f16(int D, bool causal, const CUtensorMap& tq, const CUtensorMap& tk,
                                  const CUtensorMap& tv, const CUtensorMap& tdo, const CUtensorMap& tdk,
                                  const CUtensorMap& tdv, const CUtensorMap& tdqacc, const BwdArgs& a, float* dq_acc,
@@ -2328,6 +2388,8 @@ cudaError_t launch_bwd_fused_f16(int D, bool causal, const CUtensorMap& tq, cons
                            : fused_impl<32, false>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s);
     case 64: return causal ? fused_impl<64, true>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s)
                            : fused_impl<64, false>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s);
+    case 128: return causal ? fused_impl<128, true>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s)
+                            : fused_impl<128, false>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s);
     default: return cudaErrorNotSupported;
   }
 }

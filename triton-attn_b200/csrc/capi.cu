@@ -317,7 +317,7 @@ extern "C" int tattn_bwd_fused(const void* q, const void* k, const void* v, cons
                                float sm_scale, void* stream) {
   if (!strides || !valid_dims(Z, H, N, D) || (dtype != TATTN_F16 && dtype != TATTN_F32))
     return TATTN_ERR_INVALID_ARGUMENT;
-  if (dtype != TATTN_F16 || D > 64) return TATTN_ERR_UNSUPPORTED;
+  if (dtype != TATTN_F16) return TATTN_ERR_UNSUPPORTED;
   if (int64_t(Z) * H * N == 0) return TATTN_OK;
   if (!q || !k || !v || !o || !dout || !dq || !dk || !dv || !m || !delta || !dq_acc) return TATTN_ERR_INVALID_ARGUMENT;
   DeviceState* st;
@@ -355,15 +355,17 @@ extern "C" int tattn_bwd_fused(const void* q, const void* k, const void* v, cons
                         static_cast<const void*>(dq_acc)})
     if ((reinterpret_cast<uintptr_t>(p) & 15u) != 0) return TATTN_ERR_LAYOUT;
   CUtensorMap tq, tk, tv, tdo, tdk, tdv, tdqacc;
-  // Key tiles and query blocks of 128 rows.
-  if ((rc = encode_f16(&tq, q, a.sq, Z, H, N, D, 128)) != TATTN_OK) return rc;
+  // 128-row key tiles; query blocks of 128 rows (64 at D = 128). The dQ workspace is added to in boxes
+  // of D/2 columns (32 at D = 128, where each warp holds 32 head dims of 32 queries).
+  const int q_rows = bwd_fused_query_rows(D), acc_cols = D == 128 ? 32 : D / 2;
+  if ((rc = encode_f16(&tq, q, a.sq, Z, H, N, D, q_rows)) != TATTN_OK) return rc;
   if ((rc = encode_f16(&tk, k, a.sk, Z, H, N, D, 128)) != TATTN_OK) return rc;
   if ((rc = encode_f16(&tv, v, a.sv, Z, H, N, D, 128)) != TATTN_OK) return rc;
-  if ((rc = encode_f16(&tdo, dout, a.sdo, Z, H, N, D, 128)) != TATTN_OK) return rc;
+  if ((rc = encode_f16(&tdo, dout, a.sdo, Z, H, N, D, q_rows)) != TATTN_OK) return rc;
   const Strides4 dense{int64_t(H) * N * D, int64_t(N) * D, D, 1};
   if ((rc = encode_f16(&tdk, dk, dense, Z, H, N, D, kBwdStoreRows, D / 2)) != TATTN_OK) return rc;
   if ((rc = encode_f16(&tdv, dv, dense, Z, H, N, D, kBwdStoreRows, D / 2)) != TATTN_OK) return rc;
-  if ((rc = encode_f32_dense(&tdqacc, dq_acc, Z, H, N, D, kBwdStoreRows, D / 2)) != TATTN_OK) return rc;
+  if ((rc = encode_f32_dense(&tdqacc, dq_acc, Z, H, N, D, kBwdStoreRows, acc_cols)) != TATTN_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((rc = cuda_rc(launch_bwd_preprocess(D, true, a, s))) != TATTN_OK) return rc;  // delta, zeroed dq_acc
   return cuda_rc(launch_bwd_fused_f16(D, causal != 0, tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s));

@@ -61,17 +61,19 @@ cudaError_t launch_bwd_dq_f16(int D, bool causal, int variant, const CUtensorMap
 cudaError_t launch_bwd_dkdv_f16(int D, bool causal, int variant, const CUtensorMap& tq, const CUtensorMap& tk,
                                 const CUtensorMap& tv, const CUtensorMap& tdo, const CUtensorMap& tdk,
                                 const CUtensorMap& tdv, const BwdArgs& a, cudaStream_t s);
-// Fused backward (dK, dV and dQ in one kernel; D <= 64, causal or not): tq/tdo with 128-row boxes, tk/tv
-// 128-row boxes, tdk/tdv store maps as above, tdqacc a reduce map over the dense fp32 workspace dq_acc
-// [Z, H, N, D] (kBwdStoreRows-row boxes of D/2 columns), zeroed beforehand (launch_bwd_preprocess with
-// a.dq_acc set). Runs the kernel, then writes a.dq = sm_scale * dq_acc as fp16. cudaErrorNotSupported
-// for D = 128.
+// Fused backward (dK, dV and dQ in one kernel; any supported D, causal or not): tq/tdo with boxes of
+// bwd_fused_query_rows(D) rows, tk/tv 128-row boxes, tdk/tdv store maps of kBwdStoreRows-row boxes of
+// D/2 columns, tdqacc a reduce map over the dense fp32 workspace dq_acc [Z, H, N, D] (kBwdStoreRows-row
+// boxes of D/2 columns; 32 columns at D = 128), zeroed beforehand (launch_bwd_preprocess with a.dq_acc
+// set). Runs the kernel, then writes a.dq = sm_scale * dq_acc as fp16.
 cudaError_t launch_bwd_fused_f16(int D, bool causal, const CUtensorMap& tq, const CUtensorMap& tk,
                                  const CUtensorMap& tv, const CUtensorMap& tdo, const CUtensorMap& tdk,
                                  const CUtensorMap& tdv, const CUtensorMap& tdqacc, const BwdArgs& a, float* dq_acc,
                                  cudaStream_t s);
 // Box height of the backward's output store maps (one warp's 32 TMEM lanes).
 constexpr int kBwdStoreRows = 32;
+// Query rows per block of the fused backward (its Q / dO box height): 128, or 64 at D = 128.
+constexpr int bwd_fused_query_rows(int D) { return D == 128 ? 64 : 128; }
 
 // SIMT kernels (fp32 inputs; any strides).
 cudaError_t launch_fwd_f32(int D, bool causal, const void* q, const void* k, const void* v, Strides4 sq,

@@ -25,7 +25,7 @@ from tattn import _lib
 # reference's autotune spaces (kernels.py:21-41): "BLOCK_M" is the rows a CTA owns (the forward's two
 # 128-row query tiles; the backward's 128-row key or query tile), "BLOCK_N" the rows of each inner block
 # it loops over, "num_stages" the depth of the TMA ring. "bwd" covers the split backward (dK/dV and dQ
-# kernels); the fused backward (the default for fp16, D <= 64) has one shape. This copy of the library's
+# kernels); the fused backward (the default for fp16) has one shape per head dim. This copy of the library's
 # table (csrc/tiles.h) is checked against tattn_tile_config_info by the CPU tests.
 TILE_CONFIGS: dict[str, list[dict[str, int]]] = {
     "fwd": [
@@ -156,8 +156,8 @@ def _forward(
     return o, m
 
 
-# The fp16 backward with D <= 64 runs as one fused kernel (tattn_bwd_fused) unless this is False; the
-# two-kernel path (tattn_bwd_dkdv + tattn_bwd_dq, the reference's split) is used otherwise.
+# The fp16 backward runs as one fused kernel (tattn_bwd_fused) unless this is False; the two-kernel
+# path (tattn_bwd_dkdv + tattn_bwd_dq, the reference's split) is used otherwise.
 FUSED_BACKWARD = True
 
 
@@ -165,8 +165,8 @@ def _backward(
     q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor, m: torch.Tensor, do: torch.Tensor,
     causal: bool, scale: float, config: dict[str, int] | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:  # fmt: skip
-    """Returns contiguous (dq, dk, dv): preprocess -> dK/dV -> dQ, as api.py:102-146 (for fp16, D <= 64 and
-    no explicit tile config: the same results from the fused backward, tattn_bwd_fused)."""
+    """Returns contiguous (dq, dk, dv): preprocess -> dK/dV -> dQ, as api.py:102-146 (for fp16 with no
+    explicit tile config: the same results from the fused backward, tattn_bwd_fused)."""
     _require_cuda(q)
     lib = _lib.load()
     z, h, n, d = q.shape
@@ -183,7 +183,7 @@ def _backward(
     code, stream, causal_i, sc = _dtype_code(q), _stream(q), int(bool(causal)), float(scale)
     qkvdo = _lib.strides_array(_strides(q), _strides(k), _strides(v), _strides(do))
     with torch.cuda.device(q.device):
-        if FUSED_BACKWARD and config is None and code == 0 and d <= 64:
+        if FUSED_BACKWARD and config is None and code == 0:
             # One call: delta, then one kernel for dQ, dK and dV (scores and exponentials computed once);
             # dQ is summed in an fp32 workspace. Other shapes, and explicit tile configs, take the
             # reference's three-kernel path below.
