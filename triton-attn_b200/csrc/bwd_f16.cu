@@ -1753,8 +1753,8 @@ template <int D>
 struct FusedCfg {
   using G = Geo<D>;
   // D = 128: 64-query blocks, and the dQ part computed transposed (dQ^T = K^T dS^T: 128 head-dim lanes x
-  // 64 query columns), so that S^T, dP^T, P^T, dV, dK and the dQ part still fit TMEM's 512 columns
-  // (64 + 64 + 32 + 128 + 128 + 64 = 480); with 128-query blocks and dQ = dS K they would need 704.
+  // 64 query columns), so that S^T, dP^T, P^T, dV, dK, the dQ part and dS^T fit TMEM's 512 columns
+  // (64 + 64 + 32 + 128 + 128 + 64 + 32); with 128-query blocks and dQ = dS K they would need 704.
   static constexpr bool DQT = D == 128;
   static constexpr int BQ = DQT ? 64 : 128, H = BQ / 2;  // query rows per block, columns per warpgroup
   static constexpr int NS = DQT ? 2 : 3;                  // Q/dO ring stages (shared memory)
@@ -1796,7 +1796,11 @@ struct FusedCfg {
   static constexpr uint32_t T_ST = 0, T_DPT = BQ;
   static constexpr uint32_t T_DV = DQT ? 128 : 320, T_DK = T_DV + D, T_DQ = T_DK + D;
   static constexpr uint32_t T_PT = DQT ? T_DQ + DQC : 256;
+  // D = 128: dS^T also in TMEM (fp16 pairs, after P^T), the A operand of the dK MMA, which then reads only
+  // Q from shared memory (measured +2% over reading dS^T back from shared memory).
+  static constexpr uint32_t T_DST = T_PT + BQ / 2;
   static_assert(T_DQ + DQC <= 512 && T_PT + BQ / 2 <= 512 && (DQT || T_PT + BQ / 2 <= T_DV), "TMEM budget");
+  static_assert(!DQT || T_DST + BQ / 2 <= 512, "TMEM budget");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
   static_assert(OFF_DS % 1024 == 0 && OFF_STG % 1024 == 0 && OFF_MD % 128 == 0 && OFF_ONES % 128 == 0,
                 "alignment");
@@ -2095,11 +2099,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t acc = c > 0 ? 1u : 0u;
           // dV += P^T dO (A = P^T from TMEM)
           mma_tmem_mn<D, BQ / 16>(tmem + C::T_DV, tmem + C::T_PT, dDOmn + so, C::IDESC_ACC, acc);
-          // dK += dS^T Q (A = dS^T, K-major over queries: 64-query chunks, 32 bytes per K step)
+          // dK += dS^T Q (A = dS^T from TMEM at D = 128; otherwise from shared memory, K-major over
+          // queries: 64-query chunks, 32 bytes per K step)
+          if constexpr (C::DQT) {
+            mma_tmem_mn<D, BQ / 16>(tmem + C::T_DK, tmem + C::T_DST, dQmn + so, C::IDESC_ACC, acc);
+          } else {
 #pragma unroll
-          for (int kk = 0; kk < BQ / 16; ++kk)
-            mma_f16_ss_elect(tmem + C::T_DK, dDSk + uint64_t(((kk / 4) * C::DS_CHUNK + (kk % 4) * 32) >> 4),
-                             dQmn + so + uint64_t((kk * 16 * G::SWB) >> 4), C::IDESC_ACC, kk > 0 ? 1u : acc);
+            for (int kk = 0; kk < BQ / 16; ++kk)
+              mma_f16_ss_elect(tmem + C::T_DK, dDSk + uint64_t(((kk / 4) * C::DS_CHUNK + (kk % 4) * 32) >> 4),
+                               dQmn + so + uint64_t((kk * 16 * G::SWB) >> 4), C::IDESC_ACC, kk > 0 ? 1u : acc);
+          }
           // dQ_part = dS K (A = dS, MN-major: 16 key rows of 128 bytes per K step; B = K, MN-major) or, D =
           // 128, dQ_part^T = K^T dS^T (the same two tiles as A = K^T and B = dS^T), once the compute warps
           // hold the previous block's dQ part.
@@ -2187,6 +2196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
         }
         tmem_store_cols<H / 2>(tl + C::T_PT + w * (H / 2), pt);
+        if constexpr (C::DQT) tmem_store_cols<H / 2>(tl + C::T_DST + w * (H / 2), dst);
 #pragma unroll
         for (int u = 0; u < DS_U; ++u) {
           const uint32_t addr = ds_row + uint32_t(((ds_u0 + u) ^ (r & 7)) << 4);
