@@ -308,7 +308,7 @@ def _isolated_kernel_times(q, k, v, do, causal, scale, iters: int) -> dict:
         "dq": lambda: lib.tattn_bwd_dq(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), dq.data_ptr(),
                                        m.data_ptr(), delta.data_ptr(), st, z, h, n, d, 0, ci, scale, 0, stream),
     }  # fmt: skip
-    ws = torch.empty((z, h, n, d), device=q.device, dtype=torch.float32)
+    ws = torch.empty(lib.tattn_bwd_fused_workspace_bytes(z, h, n, d), device=q.device, dtype=torch.uint8)
     st5 = _lib.strides_array(q.stride(), k.stride(), v.stride(), o.stride(), do.stride())
     calls["bwd_fused"] = lambda: lib.tattn_bwd_fused(
         q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), dq.data_ptr(), dk.data_ptr(),

@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define TATTN_ABI_VERSION 2
+#define TATTN_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define TATTN_API __attribute__((visibility("default")))
@@ -90,17 +90,23 @@ TATTN_API int tattn_bwd_dq(const void* q, const void* k, const void* v, const vo
  * caller's fp32 [Z, H, N] buffer, then dQ, dK and dV in one pass in which each (key block, query
  * block) pair's scores, P and dS are computed once; the reference's two kernels (src/tattn/kernels.py:
  * 151-239 and 242-321, launched at api.py:122-145) each recompute S and dO V^T. dQ is accumulated by
- * fp32 additions at L2 into dq_acc, a caller-provided dense fp32 [Z, H, N, D] workspace (16-byte
- * aligned; zeroed here), then scaled into dq; the order of those additions varies from run to run, so
- * dq is not bitwise reproducible (dk and dv are). strides: 20 int64 = q, k, v, o, dout each
- * (z, h, n, d); dq, dk, dv dense [Z, H, N, D].
+ * fp32 additions at L2 into `workspace` (caller-provided, tattn_bwd_fused_workspace_bytes bytes,
+ * 16-byte aligned; zeroed by the first kernel): dense fp32 [Z, H, N, D] sums, then a grid-barrier
+ * counter. The second kernel is one cooperative launch (one CTA per SM at most, all resident): once
+ * every CTA's additions have completed it scales the sums into dq itself. The order of the additions
+ * varies from run to run, so dq is not bitwise reproducible (dk and dv are).
+ * strides: 20 int64 = q, k, v, o, dout each (z, h, n, d); dq, dk, dv dense [Z, H, N, D].
  * fp16 only (every supported D, causal or not; at D = 128 the query blocks are 64 rows and each block's
  * dQ part is computed transposed, dQ^T = K^T dS^T, to fit tensor memory): fp32 requests return
  * TATTN_ERR_UNSUPPORTED (use the three calls). */
 TATTN_API int tattn_bwd_fused(const void* q, const void* k, const void* v, const void* o, const void* dout,
-                    void* dq, void* dk, void* dv, const float* m, float* delta, float* dq_acc,
+                    void* dq, void* dk, void* dv, const float* m, float* delta, void* workspace,
                     const int64_t* strides, int Z, int H, int N, int D, int dtype, int causal, float sm_scale,
                     void* stream);
+
+/* Bytes of the workspace tattn_bwd_fused needs for a [Z, H, N, D] call (a multiple of 16), or -1 for
+ * invalid dimensions. */
+TATTN_API int64_t tattn_bwd_fused_workspace_bytes(int Z, int H, int N, int D);
 
 /* Largest Z*H*N accepted by tattn_bwd_noalloc (its fixed fp32 row buffer: 16 MiB per GPU). */
 #define TATTN_BWD_NOALLOC_MAX_ROWS 4194304

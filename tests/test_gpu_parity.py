@@ -277,7 +277,7 @@ def test_entry_points_on_a_thread_that_has_not_used_cuda() -> None:
     dq_ref, dk_ref, dv_ref = api._backward(q, k, v, o_ref, m_ref, do, True, scale)
     o, dq, dk, dv = (torch.empty_like(q) for _ in range(4))
     m, delta = (torch.empty(shape[:3], device=q.device, dtype=torch.float32) for _ in range(2))
-    ws = torch.empty(shape, device=q.device, dtype=torch.float32)
+    ws = torch.empty(lib.tattn_bwd_fused_workspace_bytes(*shape), device=q.device, dtype=torch.uint8)
     stream = torch.cuda.current_stream().cuda_stream
     torch.cuda.synchronize()
     st = [t.stride() for t in (q, k, v, o, do)]

@@ -66,6 +66,7 @@ constexpr int kProducerRegs = 72;
 constexpr int kFusedComputeRegs = 208;
 constexpr int kFusedProducerRegs = 88;
 static_assert(256 * kFusedComputeRegs + 128 * kFusedProducerRegs == 384 * 168, "register split");
+
 constexpr int kTmaWarp = 8, kMmaSWarp = 9, kMmaAccWarp = 10, kAllocWarp = 11;
 constexpr unsigned long long kDrainNs = 100ull * 1000ull * 1000ull;
 
@@ -1853,6 +1854,71 @@ __device__ __forceinline__ void fused_dqt_out(const uint32_t* o, uint32_t stg, c
   }
 }
 
+// Barrier over all CTAs of a cooperative launch (all CTAs are resident, so every arrival comes), called
+// by the `nthreads` threads of the CTA that take part (named barrier `bar_id`; thread 0 of them first).
+// Thread 0 publishes the writes the participants made before the call (release), counts the CTA in and
+// waits (acquire) until `target` arrivals are counted, for at most ab.limit_ns: after that it records
+// kStatusWaitTimeout, raises the CTA's abort flag and stops waiting. A CTA whose abort flag is already up
+// still arrives (so that no other CTA waits for it) but does not wait. Returns whether the CTA may go on.
+__device__ __forceinline__ bool grid_barrier(unsigned* ctr, unsigned target, const CtaAbort& ab, int bar_id,
+                                             int nthreads, bool first) {
+  asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(nthreads) : "memory");
+  if (first) {
+    __threadfence();
+    atomicAdd(ctr, 1u);
+    const unsigned long long t0 = globaltimer_ns();
+    while (*ab.flag == 0) {
+      unsigned v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+      if (v >= target) break;
+      if (globaltimer_ns() - t0 > ab.limit_ns) {
+        *ab.flag = 1;
+        atomicOr(ab.status, kStatusWaitTimeout);
+        break;
+      }
+      __nanosleep(128);
+    }
+  }
+  asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(nthreads) : "memory");
+  return *ab.flag == 0;
+}
+
+// Last phase of the fused backward, grid-stride over threads [0, nthreads) of every CTA: dq = sm_scale *
+// dq_acc as fp16, 8 elements a thread. The thread and CTA indices are read here again: otherwise the
+// compiler keeps them in registers through the whole main loop, and the compute warps spill.
+template <int D>
+__device__ __forceinline__ void fused_dq_epilogue(const BwdArgs& a, int nthreads) {
+  unsigned t, cta;
+  asm volatile("mov.u32 %0, %%tid.x;" : "=r"(t));
+  asm volatile("mov.u32 %0, %%ctaid.x;" : "=r"(cta));
+  const int64_t n8 = int64_t(a.Z) * a.H * a.N * (D / 8);
+  const float4* acc = reinterpret_cast<const float4*>(a.dq_acc);
+  uint4* dq = static_cast<uint4*>(a.dq);
+  const float sc = a.sm_scale;
+  // U groups of 8 a thread per step, all loads issued before any store (the compiler may not move the
+  // loads past the stores itself): enough bytes in flight per SM to run at HBM speed.
+  constexpr int U = 8;
+  const int64_t stride = int64_t(gridDim.x) * nthreads;
+  for (int64_t i0 = int64_t(cta) * nthreads + t; i0 < n8; i0 += stride * U) {
+    float4 x[U], y[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i < n8) {
+        x[u] = __ldcg(acc + 2 * i);
+        y[u] = __ldcg(acc + 2 * i + 1);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i < n8)
+        dq[i] = make_uint4(pack_half2(x[u].x * sc, x[u].y * sc), pack_half2(x[u].z * sc, x[u].w * sc),
+                           pack_half2(y[u].x * sc, y[u].y * sc), pack_half2(y[u].z * sc, y[u].w * sc));
+    }
+  }
+}
+
 template <int D, bool CAUSAL>
 __global__ void __launch_bounds__(kThreads, 1)
     bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -2276,8 +2342,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    if (lane == 0) tma_store_wait_all();  // staging must stay valid until the stores and reduces are done
+    if (lane == 0) {
+      tma_store_wait_all();  // staging must stay valid until the stores and reduces are done
+      asm volatile("fence.proxy.async.global;" ::: "memory");  // the completed reduce-adds before the barrier
+    }
     __syncwarp();
+    // Last phase, once every CTA's dQ additions have completed: dq = sm_scale * dq_acc, by the compute
+    // warps of all CTAs (named barrier 1 over their 256 threads).
+    if (grid_barrier(args.grid_sync, gridDim.x, ab, 1, 256, threadIdx.x == 0))
+      fused_dq_epilogue<D>(args, 256);
   }
 
   tc_fence_before();
@@ -2288,20 +2361,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// dq = sm_scale * acc (dense [Z, H, N, D]; fp32 workspace to fp16), 8 elements per thread.
-__global__ void __launch_bounds__(256) dq_convert_kernel(const float4* __restrict__ acc, uint4* __restrict__ dq,
-                                                         long long n8, float scale) {
-  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < n8; i += (long long)gridDim.x * 256) {
-    const float4 a = acc[2 * i], b = acc[2 * i + 1];
-    dq[i] = make_uint4(pack_half2(a.x * scale, a.y * scale), pack_half2(a.z * scale, a.w * scale),
-                       pack_half2(b.x * scale, b.y * scale), pack_half2(b.z * scale, b.w * scale));
-  }
-}
-
 template <int D, bool CAUSAL>
 cudaError_t fused_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tdo,
                        const CUtensorMap& tdk, const CUtensorMap& tdv, const CUtensorMap& tdqacc, const BwdArgs& a,
-                       float* dq_acc, cudaStream_t s) {
+                       cudaStream_t s) {
   auto kern = bwd_fused_kernel<D, CAUSAL>;
   constexpr int smem = FusedCfg<D>::SMEM_BYTES;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -2310,16 +2373,15 @@ cudaError_t fused_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUten
   const long long tiles = nct * a.Z * a.H;
   if (tiles <= 0) return cudaSuccess;
   if (tiles > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-  const long long count = (long long)a.Z * a.H * a.N * D;
   const long long units = CAUSAL ? (nct + 1) / 2 * a.Z * a.H : tiles;  // the kernel's next_tile units
+  // One CTA per SM at most (shared memory), so a cooperative launch keeps every CTA resident: the grid
+  // barrier before the kernel's last phase needs that (its counter is zeroed by the preprocess).
   const unsigned grid = unsigned(units < sm_count() ? units : sm_count());
-  kern<<<dim3(grid), dim3(kThreads), smem, s>>>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  const long long n8 = count / 8;  // D is a multiple of 8
-  const unsigned cgrid = unsigned(n8 / 256 + 1 < 4LL * sm_count() ? n8 / 256 + 1 : 4LL * sm_count());
-  dq_convert_kernel<<<cgrid, 256, 0, s>>>(reinterpret_cast<const float4*>(dq_acc), reinterpret_cast<uint4*>(a.dq),
-                                          n8, a.sm_scale);
-  return cudaGetLastError();
+  BwdArgs args = a;
+  CUtensorMap m[7] = {tq, tk, tv, tdo, tdk, tdv, tdqacc};
+  void* params[8] = {&m[0], &m[1], &m[2], &m[3], &m[4], &m[5], &m[6], &args};
+  e = cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(kThreads), params, smem, s);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace
@@ -2389,17 +2451,16 @@ static_assert(FusedCfg<64>::BQ == bwd_fused_query_rows(64) && FusedCfg<128>::BQ 
 
 cudaError_t launch_bwd_fused_f16(int D, bool causal, const CUtensorMap& tq, const CUtensorMap& tk,
                                  const CUtensorMap& tv, const CUtensorMap& tdo, const CUtensorMap& tdk,
-                                 const CUtensorMap& tdv, const CUtensorMap& tdqacc, const BwdArgs& a, float* dq_acc,
-                                 cudaStream_t s) {
+                                 const CUtensorMap& tdv, const CUtensorMap& tdqacc, const BwdArgs& a, cudaStream_t s) {
   switch (D) {
-    case 16: return causal ? fused_impl<16, true>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s)
-                           : fused_impl<16, false>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s);
-    case 32: return causal ? fused_impl<32, true>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s)
-                           : fused_impl<32, false>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s);
-    case 64: return causal ? fused_impl<64, true>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s)
-                           : fused_impl<64, false>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s);
-    case 128: return causal ? fused_impl<128, true>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s)
-                            : fused_impl<128, false>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s);
+    case 16: return causal ? fused_impl<16, true>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, s)
+                           : fused_impl<16, false>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, s);
+    case 32: return causal ? fused_impl<32, true>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, s)
+                           : fused_impl<32, false>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, s);
+    case 64: return causal ? fused_impl<64, true>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, s)
+                           : fused_impl<64, false>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, s);
+    case 128: return causal ? fused_impl<128, true>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, s)
+                            : fused_impl<128, false>(tq, tk, tv, tdo, tdk, tdv, tdqacc, a, s);
     default: return cudaErrorNotSupported;
   }
 }

@@ -312,14 +312,16 @@ extern "C" int tattn_bwd_dq(const void* q, const void* k, const void* v, const v
 }
 
 extern "C" int tattn_bwd_fused(const void* q, const void* k, const void* v, const void* o, const void* dout,
-                               void* dq, void* dk, void* dv, const float* m, float* delta, float* dq_acc,
+                               void* dq, void* dk, void* dv, const float* m, float* delta, void* workspace,
                                const int64_t* strides, int Z, int H, int N, int D, int dtype, int causal,
                                float sm_scale, void* stream) {
   if (!strides || !valid_dims(Z, H, N, D) || (dtype != TATTN_F16 && dtype != TATTN_F32))
     return TATTN_ERR_INVALID_ARGUMENT;
   if (dtype != TATTN_F16) return TATTN_ERR_UNSUPPORTED;
   if (int64_t(Z) * H * N == 0) return TATTN_OK;
-  if (!q || !k || !v || !o || !dout || !dq || !dk || !dv || !m || !delta || !dq_acc) return TATTN_ERR_INVALID_ARGUMENT;
+  if (!q || !k || !v || !o || !dout || !dq || !dk || !dv || !m || !delta || !workspace)
+    return TATTN_ERR_INVALID_ARGUMENT;
+  float* dq_acc = static_cast<float*>(workspace);
   DeviceState* st;
   int rc = device_setup(&st);
   if (rc != TATTN_OK) return rc;
@@ -340,6 +342,7 @@ extern "C" int tattn_bwd_fused(const void* q, const void* k, const void* v, cons
   a.dk = dk;
   a.dv = dv;
   a.dq_acc = dq_acc;
+  a.grid_sync = reinterpret_cast<unsigned*>(static_cast<char*>(workspace) + int64_t(Z) * H * N * D * 4);
   a.Z = Z;
   a.H = H;
   a.N = N;
@@ -367,8 +370,13 @@ extern "C" int tattn_bwd_fused(const void* q, const void* k, const void* v, cons
   if ((rc = encode_f16(&tdv, dv, dense, Z, H, N, D, kBwdStoreRows, D / 2)) != TATTN_OK) return rc;
   if ((rc = encode_f32_dense(&tdqacc, dq_acc, Z, H, N, D, kBwdStoreRows, acc_cols)) != TATTN_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if ((rc = cuda_rc(launch_bwd_preprocess(D, true, a, s))) != TATTN_OK) return rc;  // delta, zeroed dq_acc
-  return cuda_rc(launch_bwd_fused_f16(D, causal != 0, tq, tk, tv, tdo, tdk, tdv, tdqacc, a, dq_acc, s));
+  if ((rc = cuda_rc(launch_bwd_preprocess(D, true, a, s))) != TATTN_OK) return rc;  // delta, zeroed workspace
+  return cuda_rc(launch_bwd_fused_f16(D, causal != 0, tq, tk, tv, tdo, tdk, tdv, tdqacc, a, s));
+}
+
+extern "C" int64_t tattn_bwd_fused_workspace_bytes(int Z, int H, int N, int D) {
+  if (!valid_dims(Z, H, N, D) || double(Z) * H * N * (4.0 * D + 4.0) > 4e18) return -1;
+  return bwd_fused_workspace_bytes(Z, H, N, D);
 }
 
 namespace tattn {

@@ -33,6 +33,7 @@ struct BwdArgs {
   // outputs (dense [Z, H, N, D])
   void* dq; void* dk; void* dv;
   float* dq_acc;     // fused backward: dense fp32 [Z, H, N, D] dQ workspace (zeroed by the preprocess), or null
+  unsigned* grid_sync;  // fused backward: its grid-barrier counter (zeroed by the preprocess), or null
   int Z, H, N;
   float sm_scale;    // signed
   float qk_scale;    // |sm_scale| * log2(e)
@@ -61,19 +62,21 @@ cudaError_t launch_bwd_dq_f16(int D, bool causal, int variant, const CUtensorMap
 cudaError_t launch_bwd_dkdv_f16(int D, bool causal, int variant, const CUtensorMap& tq, const CUtensorMap& tk,
                                 const CUtensorMap& tv, const CUtensorMap& tdo, const CUtensorMap& tdk,
                                 const CUtensorMap& tdv, const BwdArgs& a, cudaStream_t s);
-// Fused backward (dK, dV and dQ in one kernel; any supported D, causal or not): tq/tdo with boxes of
-// bwd_fused_query_rows(D) rows, tk/tv 128-row boxes, tdk/tdv store maps of kBwdStoreRows-row boxes of
-// D/2 columns, tdqacc a reduce map over the dense fp32 workspace dq_acc [Z, H, N, D] (kBwdStoreRows-row
-// boxes of D/2 columns; 32 columns at D = 128), zeroed beforehand (launch_bwd_preprocess with a.dq_acc
-// set). Runs the kernel, then writes a.dq = sm_scale * dq_acc as fp16.
+// Fused backward kernel (any supported D, causal or not; one cooperative launch): dK, dV and the dQ
+// sums into the fp32 workspace a.dq_acc [Z, H, N, D], then a grid barrier and a.dq = sm_scale * dq_acc
+// as fp16. a.dq_acc, a.delta and the barrier counter a.grid_sync come from launch_bwd_preprocess.
+// tq/tdo with boxes of bwd_fused_query_rows(D) rows, tk/tv 128-row boxes, tdk/tdv store maps of
+// kBwdStoreRows-row boxes of D/2 columns, tdqacc a reduce map over a.dq_acc (kBwdStoreRows-row boxes
+// of D/2 columns; 32 columns at D = 128).
 cudaError_t launch_bwd_fused_f16(int D, bool causal, const CUtensorMap& tq, const CUtensorMap& tk,
                                  const CUtensorMap& tv, const CUtensorMap& tdo, const CUtensorMap& tdk,
-                                 const CUtensorMap& tdv, const CUtensorMap& tdqacc, const BwdArgs& a, float* dq_acc,
-                                 cudaStream_t s);
+                                 const CUtensorMap& tdv, const CUtensorMap& tdqacc, const BwdArgs& a, cudaStream_t s);
 // Box height of the backward's output store maps (one warp's 32 TMEM lanes).
 constexpr int kBwdStoreRows = 32;
 // Query rows per block of the fused backward (its Q / dO box height): 128, or 64 at D = 128.
-constexpr int bwd_fused_query_rows(int D) { return D == 128 ? 64 : 128; }
+__host__ __device__ constexpr int bwd_fused_query_rows(int D) { return D == 128 ? 64 : 128; }
+// Workspace of tattn_bwd_fused: the fp32 dQ rows [Z, H, N, D], then 16 bytes for the grid-barrier counter.
+inline int64_t bwd_fused_workspace_bytes(int Z, int H, int N, int D) { return int64_t(Z) * H * N * D * 4 + 16; }
 
 // SIMT kernels (fp32 inputs; any strides).
 cudaError_t launch_fwd_f32(int D, bool causal, const void* q, const void* k, const void* v, Strides4 sq,
@@ -81,8 +84,8 @@ cudaError_t launch_fwd_f32(int D, bool causal, const void* q, const void* k, con
 cudaError_t launch_bwd_dq_f32(int D, bool causal, const BwdArgs& a, cudaStream_t s);
 cudaError_t launch_bwd_dkdv_f32(int D, bool causal, const BwdArgs& a, cudaStream_t s);
 
-// delta = rowsum(dO * O) in fp32 (fp16 or fp32 inputs).
-// delta = rowsum(dO * O); also zeroes the rows of a.dq_acc when it is set.
+// delta = rowsum(dO * O) in fp32 (fp16 or fp32 inputs); also zeroes the rows of a.dq_acc and the
+// counter a.grid_sync when they are set (the fused backward's workspace).
 cudaError_t launch_bwd_preprocess(int D, bool is_f16, const BwdArgs& a, cudaStream_t s);
 
 }  // namespace tattn

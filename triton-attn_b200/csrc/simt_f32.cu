@@ -322,6 +322,7 @@ __global__ void __launch_bounds__(256) preprocess_kernel(BwdArgs a) {
 #pragma unroll
     for (int e = 0; e < D / L / 4; ++e) dst[e] = make_uint4(0u, 0u, 0u, 0u);
   }
+  if (a.grid_sync != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *a.grid_sync = 0u;  // its grid barrier
 }
 
 template <int D>

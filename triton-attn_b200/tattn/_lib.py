@@ -29,6 +29,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tattn_bwd_dq": (_I, [_P, _P, _P, _P, _P, _P, _P, _I64P, _I, _I, _I, _I, _I, _I, _F, _I, _P]),
     "tattn_bwd_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64P, _I, _I, _I, _I, _I, _I, _F, _P]),
     "tattn_bwd_fused": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64P, _I, _I, _I, _I, _I, _I, _F, _P]),
+    "tattn_bwd_fused_workspace_bytes": (ctypes.c_int64, [_I, _I, _I, _I]),
     "tattn_layout_ok": (_I, [_P, _I64P, _I, _I, _I, _I]),
     "tattn_selftest_exp2": (_I, [_P, _P, _P, _P, _I, _P]),
     "tattn_selftest_wait": (_I, [_P]),
@@ -42,7 +43,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tattn_status_string": (ctypes.c_char_p, [_I]),
     "tattn_abi_version": (_I, []),
 }
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

@@ -187,7 +187,7 @@ def _backward(
             # One call: delta, then one kernel for dQ, dK and dV (scores and exponentials computed once);
             # dQ is summed in an fp32 workspace. Other shapes, and explicit tile configs, take the
             # reference's three-kernel path below.
-            ws = torch.empty((z, h, n, d), device=q.device, dtype=torch.float32)
+            ws = torch.empty(lib.tattn_bwd_fused_workspace_bytes(z, h, n, d), device=q.device, dtype=torch.uint8)
             strides = _lib.strides_array(_strides(q), _strides(k), _strides(v), _strides(o), _strides(do))
             rc = lib.tattn_bwd_fused(
                 q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), dq.data_ptr(),
