@@ -66,8 +66,8 @@ L2_BYTES = 126 * 2**20
 # > L2; the command is NCU_TRAFFIC_SOURCE), divided by the captured pairs. Scaled by the pairs a launch
 # processes, as the traffic grows with them.
 NCU_TRAFFIC_PER_PAIR: dict[tuple[str, str], float] = {
-    ("cfg5", "bwd_fused"): (406_999_296 + 222_435_584) / 64,
-    ("cfg5", "fwd"): (206_485_760 + 50_135_040) / 64,
+    ("cfg5", "bwd_fused"): (540_986_368 + 303_763_712) / 64,
+    ("cfg5", "fwd"): (210_691_072 + 50_971_648) / 64,
 }
 NCU_TRAFFIC_SOURCE = ("ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum --clock-control none "
                       "-k regex:'bwd_fused|fwd_f16' -s 6 -c 2 python bench.py --lean --pairs 64 --steps 2 --warmup 3")
@@ -623,6 +623,9 @@ def run_gpu(args) -> None:
                 # the op's own tensors: backward reads q, k, v, O, dO, M and writes dq, dk, dv (the fp32 dQ
                 # workspace is the implementation's); forward reads q, k, v and writes O, M
                 "algorithmic_bytes": (8 if dom == "bwd_fused" else 4) * pairs * n * d * 2 + 4 * pairs * n,
+                # the fused kernel's fp32 dQ sums, written (reduce-adds leaving L2) and read back once for
+                # the fp16 dq: the part of `traffic` above the op's own tensors
+                "workspace_bytes": 8 * pairs * n * d if dom == "bwd_fused" else 0,
                 "flops_per_launch": kflops[dom],
                 "timing": "CUDA events around each call inside the timed steps, mean over steps, max over ranks",
             },
@@ -656,9 +659,9 @@ def run_gpu(args) -> None:
         dist.destroy_process_group()
 
 
-# Library kernels one fwd+bwd step launches: the forward; the delta pass, the fused backward kernel and
-# the dQ scaling.
-LAUNCHES_PER_STEP = 4
+# Library kernels one fwd+bwd step launches: the forward; the delta pass and the fused backward kernel
+# (which also scales dQ).
+LAUNCHES_PER_STEP = 3
 
 
 def run_compare(args) -> None:
