@@ -58,7 +58,7 @@ struct FwdCfg {
   // q_full, k_full[NS], v_full[NS], kv_empty[2][NS], s_full[2], o_done[2], exp_done[2], fin[2],
   // s_free[2], p_full[2]
   static constexpr int NBARS = 1 + 4 * NS + 12;
-  static constexpr int OFF_MISC = OFF_BAR + NBARS * 8;  // tmem base (u32), abort flag (int)
+  static constexpr int OFF_MISC = OFF_BAR + NBARS * 8;  // tmem base (u32), abort flag (int), head index (int)
   static constexpr int SMEM_USED = OFF_MISC + 16;
   // Request at least ~116 KB so exactly one CTA (which owns all 512 TMEM columns) fits per SM.
   static constexpr int SMEM_BYTES = (SMEM_USED > 118784 ? SMEM_USED : 118784) + 1024;
@@ -225,6 +225,7 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(&bar_p_full[i], 128);
     }
     *abort_flag = 0;
+    *reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8) = bh;  // for the softmax epilogue
     fence_mbar_init();
   }
   if (warp == 11) {
@@ -413,7 +414,11 @@ __global__ void __launch_bounds__(384, 1)
     if (ok && n > 0 && warp_wait(&bar_o_done[i], (n - 1) & 1, ab)) {
       tc_fence_after();
       const float inv_l = 1.f / l_run;
-      __half* orow = reinterpret_cast<__half*>(args.o) + zi * args.so.z + hi * args.so.h + int64_t(row) * args.so.n;
+      // The head index from shared memory rather than a register held through the block loop (one
+      // spilled register fewer).
+      const int bh_e = *reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);
+      const int zi_e = bh_e / args.H, hi_e = bh_e % args.H;
+      __half* orow = reinterpret_cast<__half*>(args.o) + zi_e * args.so.z + hi_e * args.so.h + int64_t(row) * args.so.n;
 #pragma unroll
       for (int c0 = 0; c0 < D; c0 += 32) {
         constexpr int W = D < 32 ? D : 32;
@@ -431,7 +436,7 @@ __global__ void __launch_bounds__(384, 1)
           for (int v = 0; v < W / 8; ++v) dst[v] = make_uint4(h[4 * v], h[4 * v + 1], h[4 * v + 2], h[4 * v + 3]);
         }
       }
-      if (row < N) args.m[int64_t(bh) * N + row] = m_run + log2f(l_run);
+      if (row < N) args.m[int64_t(bh_e) * N + row] = m_run + log2f(l_run);
     }
   }
 
