@@ -83,9 +83,11 @@ def test_tile_table_matches_the_library() -> None:
                 assert 1 <= t <= len(table)
                 assert lib.tattn_tile_supported(k, t, d) == 1
                 assert lib.tattn_tile_default(k, d, causal, _lib.TATTN_F32) == 0
-        # 128-row inner blocks do not fit TMEM at D = 128; 64-row ones fit every head dim
+        # 64-row inner blocks fit every head dim; 128-row ones at D = 128 only in the forward with a
+        # 2-stage ring (P written over S in TMEM; 4 stages of 128 x 128 K and V exceed shared memory)
         for i, cfg in enumerate(table):
-            assert lib.tattn_tile_supported(k, i + 1, 128) == (cfg["BLOCK_N"] == 64)
+            fits = cfg["BLOCK_N"] == 64 or (kind == "fwd" and cfg["num_stages"] <= 2)
+            assert lib.tattn_tile_supported(k, i + 1, 128) == fits
             assert lib.tattn_tile_supported(k, i + 1, 64) == 1
-            assert api.tile_supported(cfg, kind, 128) == (cfg["BLOCK_N"] == 64)
+            assert api.tile_supported(cfg, kind, 128) == fits
     assert lib.tattn_tile_default(0, 48, 0, _lib.TATTN_F16) == -1

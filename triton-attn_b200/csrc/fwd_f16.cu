@@ -62,10 +62,17 @@ struct FwdCfg {
   static constexpr int SMEM_USED = OFF_MISC + 16;
   // Request at least ~116 KB so exactly one CTA (which owns all 512 TMEM columns) fits per SM.
   static constexpr int SMEM_BYTES = (SMEM_USED > 118784 ? SMEM_USED : 118784) + 1024;
-  static constexpr uint32_t TM_S = 0;                   // + i * BN
-  static constexpr uint32_t TM_P = 2 * BN;              // + i * BN / 2
-  static constexpr uint32_t TM_O = 3 * BN;              // + i * D
-  static_assert(3 * BN + 2 * D <= 512, "TMEM budget");
+  // TMEM: S_i [BN], P_i [BN / 2, fp16 pairs], O_i [D] per tile. Where S, P and O of both tiles do not
+  // fit 512 columns (D = 128 with 128-key blocks), P_i is written over the first half of S_i (ALIAS_P):
+  // the MMAs of a CTA run in issue order, so S_i(j + 1), issued after PV_i(j), overwrites P_i(j) only
+  // once PV_i(j) has read it.
+  static constexpr bool ALIAS_P = 3 * BN + 2 * D > 512;
+  static constexpr uint32_t TM_S = 0;                             // + i * BN
+  static constexpr uint32_t TM_P = ALIAS_P ? TM_S : 2 * BN;       // + i * BN (ALIAS_P) or i * BN / 2
+  static constexpr uint32_t TM_O = ALIAS_P ? 2 * BN : 3 * BN;     // + i * D
+  static constexpr uint32_t P_STRIDE = ALIAS_P ? BN : BN / 2;     // columns between P_0 and P_1
+  static_assert((ALIAS_P ? 2 * BN : 3 * BN) + 2 * D <= 512, "TMEM budget");
+  static_assert(OFF_MISC + 16 + 1024 <= 232448, "shared memory budget");
   static constexpr uint32_t IDESC_S = idesc_f16_f32(128, BN, false);
   static constexpr uint32_t IDESC_PV = idesc_f16_f32(128, D, true);
 };
@@ -292,7 +299,7 @@ __global__ void __launch_bounds__(384, 1)
       const uint64_t dQ = smem_desc(sQ, 16, 8 * C::SWB, C::LAYOUT);
       const uint64_t dK = smem_desc(sK, 16, 8 * C::SWB, C::LAYOUT);
       const uint64_t dV = smem_desc(sV, C::KCHUNK, 8 * C::SWB, C::LAYOUT);
-      const uint32_t tS = tmem + C::TM_S + i * BN, tP = tmem + C::TM_P + i * (BN / 2), tO = tmem + C::TM_O + i * D;
+      const uint32_t tS = tmem + C::TM_S + i * BN, tP = tmem + C::TM_P + i * C::P_STRIDE, tO = tmem + C::TM_O + i * D;
       bool ok = n > 0 && warp_wait(bar_q, 0, ab) && warp_wait(&bar_k_full[0], 0, ab);
       if (ok) {
         tc_fence_after();
@@ -300,6 +307,28 @@ __global__ void __launch_bounds__(384, 1)
         mma_commit_elect(&bar_s_full[i]);
       }
       for (int j = 0; ok && j < n; ++j) {
+        if (C::ALIAS_P) {
+          // PV(j) reads P(j) where S(j) was, then S(j + 1) overwrites both (in issue order).
+          if (!warp_wait(&bar_p_full[i], j & 1, ab) || !warp_wait(&bar_v_full[j % C::NS], (j / C::NS) & 1, ab)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv_stage<C, D>(j % C::NS, tO, tP, dV, j > 0 ? 1u : 0u);
+          mma_commit_elect(&bar_o_done[i]);
+          mma_commit_elect(&bar_kv_empty[i * C::NS + j % C::NS]);
+          if (j + 1 < n) {
+            const int b = j + 1;
+            if (!warp_wait(&bar_k_full[b % C::NS], (b / C::NS) & 1, ab)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_qk_stage<C, D>(b % C::NS, i, tS, dQ, dK, idesc_s);
+            mma_commit_elect(&bar_s_full[i]);
+          }
+          continue;
+        }
         if (j + 1 < n) {
           const int b = j + 1;
           if (!warp_wait(&bar_s_free[i], j & 1, ab) || !warp_wait(&bar_k_full[b % C::NS], (b / C::NS) & 1, ab)) {
@@ -332,7 +361,7 @@ __global__ void __launch_bounds__(384, 1)
     const int n = i ? n_1 : n_0;
     const uint32_t lane_off = uint32_t((warp % 4) * 32) << 16;
     const uint32_t tS = tmem + lane_off + C::TM_S + i * BN;
-    const uint32_t tP = tmem + lane_off + C::TM_P + i * (BN / 2);
+    const uint32_t tP = tmem + lane_off + C::TM_P + i * C::P_STRIDE;
     const uint32_t tO = tmem + lane_off + C::TM_O + i * D;
     const float scale = args.qk_scale;
     const uint64_t scale2 = f2(scale, scale);
@@ -346,7 +375,7 @@ __global__ void __launch_bounds__(384, 1)
       tmem_wait_ld();
       reg_fence<BN>(s);
       tc_fence_before();
-      mbar_arrive(&bar_s_free[i]);  // the tensor core may now write S(j+1) of this tile
+      if (!C::ALIAS_P) mbar_arrive(&bar_s_free[i]);  // the tensor core may now write S(j+1) of this tile
 
       // Columns past N (ragged tail) only occur in the last block; columns above the diagonal
       // (causal) in every block that reaches past the tile's first row (the last BM / BN blocks).
@@ -387,8 +416,9 @@ __global__ void __launch_bounds__(384, 1)
         l_run += last ? exp_cols<kSplit, BN, true>(s, p, scale2, negm2, lim)
                       : exp_cols<kSplit, BN, false>(s, p, scale2, negm2, lim);
 
-      // PV(j-1) must have landed before P and O of this tile are touched again.
-      if (j > 0) {
+      // PV(j-1) must have landed before P and O of this tile are touched again (ALIAS_P: it has, since
+      // S(j) was issued after it and has completed).
+      if (!C::ALIAS_P && j > 0) {
         if (!warp_wait(&bar_o_done[i], (j - 1) & 1, ab)) { ok = false; break; }
         tc_fence_after();
       }
@@ -476,8 +506,7 @@ cudaError_t launch_variant(int v, const CUtensorMap& tq, const CUtensorMap& tk, 
     case 1:
       return launch_impl<D, CAUSAL, kFwdTiles[1].block_n, kFwdTiles[1].stages>(tq, tk, tv, a, s);
     case 2:
-      if constexpr (D <= 64) return launch_impl<D, CAUSAL, kFwdTiles[2].block_n, kFwdTiles[2].stages>(tq, tk, tv, a, s);
-      break;
+      return launch_impl<D, CAUSAL, kFwdTiles[2].block_n, kFwdTiles[2].stages>(tq, tk, tv, a, s);
     default:
       break;
   }
