@@ -104,3 +104,14 @@ def test_wait_limit_is_host_state(lib: ctypes.CDLL) -> None:
         assert lib.tattn_get_wait_limit_ns() == 1_000_000_000
     finally:
         lib.tattn_set_wait_limit_ns(before)
+
+
+def test_fused_workspace_size(lib: ctypes.CDLL) -> None:
+    """tattn_bwd_fused's workspace: the fp32 dQ sums [Z, H, N, D] plus 16 bytes for its grid-barrier
+    counter; -1 for dimensions the library refuses (a bad head dim, negative sizes, an overflowing
+    product). Host arithmetic only."""
+    for z, h, n, d in ((1, 2, 333, 64), (4, 16, 4096, 128), (3, 5, 1, 16), (0, 4, 7, 32)):
+        assert lib.tattn_bwd_fused_workspace_bytes(z, h, n, d) == z * h * n * d * 4 + 16
+    assert lib.tattn_bwd_fused_workspace_bytes(1, 1, 8, 48) == -1
+    assert lib.tattn_bwd_fused_workspace_bytes(-1, 1, 8, 64) == -1
+    assert lib.tattn_bwd_fused_workspace_bytes(1 << 30, 1 << 30, 1 << 30, 64) == -1
