@@ -1514,11 +1514,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tm_do);
   }
   // Constant A operands of the folded -M / -delta K step (as in the fused kernel; bf16 1.0 = 0x3F80).
-  for (int idx = threadIdx.x; C::FOLD && idx < 2 * C::ONES_TILE / 16; idx += blockDim.x) {
-    const int t = idx / (C::ONES_TILE / 16), byte = (idx % (C::ONES_TILE / 16)) * 16;
-    const uint4 row = t == 0 ? make_uint4(0x3F803F80u, 0x00003F80u, 0u, 0u) : make_uint4(0u, 0x3F800000u, 0x3F803F80u, 0u);
-    *reinterpret_cast<uint4*>(smem + C::OFF_ONES + t * C::ONES_TILE + byte) =
-        (byte % 256) < 128 ? row : make_uint4(0u, 0u, 0u, 0u);
+  if constexpr (C::FOLD) {
+    for (int idx = threadIdx.x; idx < 2 * C::ONES_TILE / 16; idx += blockDim.x) {
+      const int t = idx / (C::ONES_TILE / 16), byte = (idx % (C::ONES_TILE / 16)) * 16;
+      const uint4 row = t == 0 ? make_uint4(0x3F803F80u, 0x00003F80u, 0u, 0u) : make_uint4(0u, 0x3F800000u, 0x3F803F80u, 0u);
+      *reinterpret_cast<uint4*>(smem + C::OFF_ONES + t * C::ONES_TILE + byte) =
+          (byte % 256) < 128 ? row : make_uint4(0u, 0u, 0u, 0u);
+    }
   }
   fence_proxy_async_smem();
   tc_fence_before();
