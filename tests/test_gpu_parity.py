@@ -263,6 +263,35 @@ def test_fused_backward_matches_three_kernel_path(d: int, causal: bool) -> None:
         _close(got, w, torch.float16, "fused grad")
 
 
+def test_side_streams_run_concurrently() -> None:
+    """Forward + backward on two side streams at once (a training loop's pattern): each call enqueues on
+    the caller's current stream, the fused backward's cooperative kernel on each stream has its own
+    workspace (and grid-barrier counter), and both match a run on the default stream bit for bit in
+    dk/dv (dq within the reduce-order tolerance)."""
+    shape, d = (2, 4, 700, 64), 64
+    scale = d**-0.5
+    ins = [[_rand(shape, torch.float16, s) for s in range(10 * t, 10 * t + 4)] for t in range(2)]
+    want = []
+    for q, k, v, do in ins:
+        o, m = api._forward(q, k, v, True, scale)
+        want.append((o, *api._backward(q, k, v, o, m, do, True, scale)))
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream() for _ in range(2)]
+    got = [None, None]
+    for _ in range(3):
+        for t, st in enumerate(streams):
+            st.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(st):
+                q, k, v, do = ins[t]
+                o, m = api._forward(q, k, v, True, scale)
+                got[t] = (o, *api._backward(q, k, v, o, m, do, True, scale))
+        torch.cuda.synchronize()
+        assert _lib.device_status() == 0
+        for g_, w_ in zip(got, want, strict=True):
+            assert torch.equal(g_[0], w_[0]) and torch.equal(g_[2], w_[2]) and torch.equal(g_[3], w_[3])
+            assert (g_[1].float() - w_[1].float()).abs().max().item() <= 2e-3
+
+
 def test_entry_points_on_a_thread_that_has_not_used_cuda() -> None:
     """Each C-ABI entry point as the first CUDA work of a new thread (the situation of the autograd
     engine's worker thread): no CUDA context is current there until the library makes the device's
