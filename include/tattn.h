@@ -152,6 +152,10 @@ TATTN_API int tattn_tile_supported(int kind, int tile_cfg, int D);
  * a test can hold the polynomial to its error bound against CUDA's own outputs. Device pointers. */
 TATTN_API int tattn_selftest_exp2(const float* x, float* y_poly, float* y_hw, float* y_lib, int n, void* stream);
 
+/* The backward's FMA-pipe exp2 (degree-4 polynomial) on n caller-given inputs: y[i] ~ 2^x[i], for
+ * tests of its error bound (2.7e-6 relative for results above 2^-24). */
+TATTN_API int tattn_selftest_exp2_poly4(const float* x, float* y, int n, void* stream);
+
 /* Bound of every wait inside the tensor-core kernels (no reference counterpart; the Triton kernels have
  * no such waits). A wait that has not completed after limit_ns nanoseconds makes its CTA give up: it
  * sets TATTN_DEV_WAIT_TIMEOUT in the device status word, drains its own copies in flight, frees its

@@ -436,3 +436,11 @@ def test_polynomial_exp2_against_cuda() -> None:
     assert rel_hw.max().item() < 1e-4, rel_hw.max().item()
     tiny = ~normal
     assert torch.isfinite(p[tiny]).all() and (p[tiny] >= 0).all() and (p[tiny] <= 2.0**-23).all()
+    # the backward's degree-4 polynomial on the same inputs
+    y4 = torch.empty_like(x)
+    _lib.check("tattn_selftest_exp2_poly4", lib.tattn_selftest_exp2_poly4(x.data_ptr(), y4.data_ptr(), x.numel(), None))
+    torch.cuda.synchronize()
+    p4 = y4.double().cpu()
+    rel4 = ((p4 - exact).abs() / exact)[normal]
+    assert rel4.max().item() < 3e-6, rel4.max().item()
+    assert torch.isfinite(p4[tiny]).all() and (p4[tiny] >= 0).all() and (p4[tiny] <= 2.0**-23).all()

@@ -112,14 +112,17 @@ __device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
 // exp2 of a pair: on MUFU, or (EMU) on the FMA pipe.
 template <bool EMU>
 __device__ __forceinline__ float2 exp2_pair(uint64_t x) {
-  if (EMU) return f2_unpack(exp2_poly_x2(x));
+  if (EMU) return f2_unpack(exp2_poly4_x2(x));  // degree 4: gradients sum P over many rows
   const float2 v = f2_unpack(x);
   return make_float2(ex2_approx(v.x), ex2_approx(v.y));
 }
-// Of every 8 column pairs, this many take exp2 on the FMA pipe (measured per kernel: the dK/dV compute
-// phase, with its M/delta loads and second fp16 pack, is issue-bound and fastest all on MUFU).
+// Of every 8 column pairs, this many take exp2 on the FMA pipe (degree-4 polynomial), the rest on MUFU.
+// Measured on the fused backward: 2 of 8 is 1.4-1.7 % faster than all on MUFU at configs 2, 3 and a
+// config-5 slice, with the same worst-case errors at full size (the polynomial's 2.7e-6 relative error
+// is below the fp16 output rounding); the degree-3 polynomial at 3 of 8 was faster too but took the
+// config-3 dK/dV error past 2e-3 (2.4e-3).
 constexpr int kDqEmuPairs = 2;
-constexpr int kDkvEmuPairs = 0;
+constexpr int kDkvEmuPairs = 2;
 
 // Write a [128, D] fp32 TMEM accumulator slice (this thread's lane, columns [c_begin, c_begin + W))
 // times `mul` as fp16 to dst[c_begin .. c_begin + W).

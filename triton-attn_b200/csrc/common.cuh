@@ -430,4 +430,23 @@ __device__ __forceinline__ uint64_t exp2_poly_x2(uint64_t x2) {
             __int_as_float(__float_as_int(pv.y) + (__float_as_int(tv.y) << 23)));
 }
 
+// The same with a degree-4 polynomial (max relative error 2.7e-6, one more packed FMA): accurate enough
+// that a gradient summed over thousands of query rows stays within the fp16 bound (the backward).
+__device__ __forceinline__ uint64_t exp2_poly4_x2(uint64_t x2) {
+  float2 x = f2_unpack(x2);
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
+  const uint64_t xc = f2(x.x, x.y);
+  const uint64_t shifter = f2(12582912.f, 12582912.f);
+  const uint64_t t = fadd2(xc, shifter);
+  const uint64_t f = fsub2(xc, fsub2(t, shifter));
+  uint64_t p = ffma2(f2(0.009570102207362652f, 0.009570102207362652f), f, f2(0.05591785907745361f, 0.05591785907745361f));
+  p = ffma2(p, f, f2(0.240247443318367f, 0.240247443318367f));
+  p = ffma2(p, f, f2(0.6931217908859253f, 0.6931217908859253f));
+  p = ffma2(p, f, f2(0.9999992847442627f, 0.9999992847442627f));
+  const float2 pv = f2_unpack(p), tv = f2_unpack(t);
+  return f2(__int_as_float(__float_as_int(pv.x) + (__float_as_int(tv.x) << 23)),
+            __int_as_float(__float_as_int(pv.y) + (__float_as_int(tv.y) << 23)));
+}
+
 }  // namespace tattn

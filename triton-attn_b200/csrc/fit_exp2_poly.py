@@ -1,10 +1,12 @@
-"""Derive the cubic used by the kernels' FMA-pipe exp2 (``exp2_poly_x2`` in common.cuh).
+"""Derive the polynomials used by the kernels' FMA-pipe exp2 (``exp2_poly_x2``, degree 3, and
+``exp2_poly4_x2``, degree 4, in common.cuh).
 
 Method: Cody-Waite style range reduction x = j + f, j = round(x), f in [-0.5, 0.5], so 2^x = 2^j * 2^f;
-2^f is approximated by the degree-3 polynomial that minimises the maximum *relative* error on
-[-0.5, 0.5], found with the Remez exchange algorithm. Printed: the coefficients (fp32, with their bit
-patterns) and the max relative error of an fp32 Horner evaluation (about 7.5e-5, below the 4.9e-4
-half-ulp of the fp16 P it feeds). Run: python triton-attn_b200/csrc/fit_exp2_poly.py
+2^f is approximated by the polynomial of the given degree that minimises the maximum *relative* error
+on [-0.5, 0.5], found with the Remez exchange algorithm. Printed per degree: the coefficients (fp32, with
+their bit patterns) and the max relative error of an fp32 Horner evaluation (about 7.5e-5 for degree 3,
+below the 4.9e-4 half-ulp of the fp16 P it feeds; 2.7e-6 for degree 4). Run:
+python triton-attn_b200/csrc/fit_exp2_poly.py
 """
 
 import numpy as np
@@ -40,16 +42,17 @@ def remez_rel(deg: int = 3, a: float = -0.5, b: float = 0.5, iters: int = 30) ->
 
 
 def main() -> None:
-    c, e = remez_rel()
-    c32 = c.astype(np.float32)
-    g = np.linspace(-0.5, 0.5, 1000001).astype(np.float32)
-    p = np.float32(c32[3])
-    for k in (2, 1, 0):
-        p = (p * g + c32[k]).astype(np.float32)
-    e32 = float(np.abs(p.astype(np.float64) / np.exp2(g.astype(np.float64)) - 1).max())
-    print(f"minimax rel err {e:.3e}; fp32 Horner rel err {e32:.3e}")
-    for i, v in enumerate(c32):
-        print(f"c{i} = {float(v)!r}f  // 0x{int(v.view(np.uint32)):08x}")
+    for deg in (3, 4):
+        c, e = remez_rel(deg)
+        c32 = c.astype(np.float32)
+        g = np.linspace(-0.5, 0.5, 1000001).astype(np.float32)
+        p = np.float32(c32[deg])
+        for k in range(deg - 1, -1, -1):
+            p = (p * g + c32[k]).astype(np.float32)
+        e32 = float(np.abs(p.astype(np.float64) / np.exp2(g.astype(np.float64)) - 1).max())
+        print(f"degree {deg}: minimax rel err {e:.3e}; fp32 Horner rel err {e32:.3e}")
+        for i, v in enumerate(c32):
+            print(f"  c{i} = {float(v)!r}f  // 0x{int(v.view(np.uint32)):08x}")
 
 
 if __name__ == "__main__":

@@ -32,6 +32,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tattn_bwd_fused_workspace_bytes": (ctypes.c_int64, [_I, _I, _I, _I]),
     "tattn_layout_ok": (_I, [_P, _I64P, _I, _I, _I, _I]),
     "tattn_selftest_exp2": (_I, [_P, _P, _P, _P, _I, _P]),
+    "tattn_selftest_exp2_poly4": (_I, [_P, _P, _I, _P]),
     "tattn_selftest_wait": (_I, [_P]),
     "tattn_set_wait_limit_ns": (_I, [_U64]),
     "tattn_get_wait_limit_ns": (_U64, []),
