@@ -75,9 +75,14 @@ def test_argument_errors_need_no_device(lib: ctypes.CDLL) -> None:
     assert bad_dtype == _lib.ERR_INVALID_ARGUMENT
     bad_tile = lib.tattn_bwd_dq(16, 16, 16, 16, 16, 16, 16, _strides(1, 1, 8, 16), 1, 1, 8, 16, 0, 0, 0.1, 99, None)
     assert bad_tile == _lib.ERR_INVALID_ARGUMENT
+    # The self-tests validate their arguments before touching a device too.
+    assert lib.tattn_selftest_exp2(None, None, None, None, -1, None) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.tattn_selftest_exp2_poly4(None, None, -1, None) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.tattn_selftest_exp2_poly4(None, None, 4, None) == _lib.ERR_INVALID_ARGUMENT
     # Empty problems are valid no-ops.
     assert lib.tattn_fwd(None, None, None, None, None, _strides(0, 1, 8, 16), 0, 1, 8, 16, 0, 0, 0.1, 0, None) == 0
     assert lib.tattn_bwd_preprocess(None, None, None, _lib.strides_array((0,) * 8), 2, 2, 0, 64, 0, None) == 0
+    assert lib.tattn_selftest_exp2_poly4(None, None, 0, None) == 0
 
 
 def test_layout_rules(lib: ctypes.CDLL) -> None:
