@@ -393,6 +393,79 @@ def test_full_size_against_fp32_definition(shape, causal, heads) -> None:
     print(json.dumps({"shape": shape, "causal": causal, "max_abs": report}))
 
 
+def _sampled_rows_ref(q, k, v, do, causal, scale, rows, keys, chunk=4096):
+    """fp32 definition at sampled positions of one (batch, head) of length N, without the N x N
+    matrix: O, M (base 2) and dq at query ``rows``; dk and dv at key ``keys``. The key gradients need
+    every row's M and delta = rowsum(dO * O), so the rows are swept in ``chunk``-row slices and each
+    slice's contribution to the sampled keys is added up."""
+    qf, kf, vf, dof = (t.float() for t in (q, k, v, do))
+    n = qf.shape[0]
+    pos = torch.arange(n, device=qf.device)
+    r = torch.tensor(rows, device=qf.device)
+    s = (qf[r] @ kf.T) * scale
+    if causal:
+        s = s.masked_fill(pos[None, :] > r[:, None], float("-inf"))
+    p = torch.softmax(s, -1)
+    o_r = p @ vf
+    m_r = torch.logsumexp(s, -1) / math.log(2.0)
+    dp = dof[r] @ vf.T
+    ds = p * (dp - (dof[r] * o_r).sum(-1, keepdim=True))
+    dq_r = (ds @ kf) * scale
+    kk = torch.tensor(keys, device=qf.device)
+    dk = torch.zeros(len(keys), qf.shape[1], device=qf.device)
+    dv = torch.zeros_like(dk)
+    for i0 in range(0, n, chunk):
+        ri = pos[i0 : i0 + chunk]
+        s = (qf[ri] @ kf.T) * scale
+        if causal:
+            s = s.masked_fill(pos[None, :] > ri[:, None], float("-inf"))
+        p = torch.softmax(s, -1)
+        delta = (dof[ri] * (p @ vf)).sum(-1, keepdim=True)
+        pk = p[:, kk]
+        dsk = pk * (dof[ri] @ vf[kk].T - delta)
+        dv += pk.T @ dof[ri]
+        dk += (dsk.T @ qf[ri]) * scale
+        del s, p
+    return o_r, m_r, dq_r, dk, dv
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_long_sequence_sampled_rows(causal: bool) -> None:
+    """N = 65,536 (longer than any BASELINE config; 1,024 query blocks per head, so the backward's
+    per-key sweep and the dQ sums run over the longest range the tests reach): O, M and dq at sampled
+    query rows, dk and dv at sampled keys, against the fp32 definition computed row-chunk by
+    row-chunk. Bound: |got - want| <= 2e-3 + 2e-3 |want| for O and the gradients, 1e-3 for M."""
+    shape = (1, 2, 65536, 64)
+    g = torch.Generator(device="cuda").manual_seed(65536 + causal)
+    q, k, v, do = (torch.randn(shape, generator=g, device="cuda").to(torch.float16) for _ in range(4))
+    scale = 0.125
+    qg, kg, vg = (t.clone().requires_grad_() for t in (q, k, v))
+    out = attention(qg, kg, vg, causal=causal, sm_scale=scale)
+    out.backward(do)
+    _, m2 = api._forward(q, k, v, causal, scale)
+    rows = [0, 1, 127, 128, 4095, 20000, 32767, 32768, 50001, 65535]
+    keys = [0, 1, 129, 8191, 30000, 65535]
+    report = {}
+    for hi in range(shape[1]):
+        ref = _sampled_rows_ref(q[0, hi], k[0, hi], v[0, hi], do[0, hi], causal, scale, rows, keys)
+        got = (
+            out[0, hi, rows].float(),
+            m2[0, hi, rows],
+            qg.grad[0, hi, rows].float(),
+            kg.grad[0, hi, keys].float(),
+            vg.grad[0, hi, keys].float(),
+        )
+        for name, gt, want in zip(("o", "m", "dq", "dk", "dv"), got, ref):
+            err = (gt - want).abs()
+            report[f"{hi}.{name}"] = err.max().item()
+            if name == "m":
+                assert err.max().item() <= 1e-3, (hi, name, report)
+            else:
+                bound = 2e-3 + 2e-3 * want.abs()
+                assert bool((err <= bound).all()), (hi, name, err.max().item(), report)
+    print(json.dumps({"shape": shape, "causal": causal, "max_abs": report}))
+
+
 def test_full_size_properties() -> None:
     """Size-independent checks at config-2 size: softmax rows sum to one (V = 1 gives O = 1) and the
     output is linear in V."""
