@@ -106,11 +106,6 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const 
   return __all_sync(0xffffffffu, ok);
 }
 
-// Named barrier over `nthreads` threads (a multiple of 32); id 0 is __syncthreads.
-__device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
-
 // ----------------------------------------------------------------------------------------------
 // TMA (no multicast anywhere in this library)
 // ----------------------------------------------------------------------------------------------
@@ -179,35 +174,8 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// D[tmem] (+)= A[smem desc] * B[smem desc]
-__device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                           uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// D[tmem] (+)= A[tmem] * B[smem desc]
-__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                           uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Arrive (once) on `bar` when every tcgen05 operation this thread issued so far has completed.
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
-}
-
+// D[tmem] (+)= A * B, A from shared memory (_ss) or TMEM (_ts), B from shared memory; commit: arrive
+// (once) on `bar` when every tcgen05 operation the electing lane issued so far has completed.
 // Warp-converged issue: every lane of the issuing warp executes these with the same (warp-uniform)
 // operands and elect.sync picks one lane (the lowest, i.e. the same lane every time while the warp is
 // converged, so the commits track that lane's MMAs). Keeping the warp converged and the descriptors
