@@ -1739,22 +1739,28 @@ cudaError_t dkdv_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtens
   }
 }
 
-// ------------------------------------------------------------------- fused backward, D <= 64
+// ------------------------------------------------------------------- fused backward, every D
 // dK, dV and dQ in one pass (non-causal, or causal with each key tile's query blocks starting at the
-// diagonal block; causal tiles are taken longest first) over each (key tile, query block) pair, so S^T, dP^T and the exponentials
-// are computed once instead of once per output kernel (the reference's split, kernels.py:151-321,
-// recomputes QK^T and dO V^T for dQ). The persistent dK/dV structure (one CTA per SM, 128-key tiles,
-// static round-robin, ring of Q/dO blocks; K double-buffered because the dQ MMAs read it to the end of
-// a tile, V single-buffered and loaded by warp 11 once the tile's last dP^T MMA has read it) plus:
-//   * dS^T goes to shared memory ([128 keys, 128 queries] fp16, 128-byte swizzle, two 64-query
-//     chunks) instead of TMEM. The same bytes are the K-major A operand of dK += dS^T Q and the
-//     MN-major A operand of dQ_part = dS K (rows = keys, 128 contiguous bytes = 64 queries).
-//   * dQ_part of a block (128 queries x D, fp32) is accumulated in TMEM by its own MMAs; the compute
-//     warps read it one block later, right after handing over the next block's P^T/dS^T (the dQ MMAs
-//     of that block wait for the read: dq_read), and add it into a dense fp32 workspace through TMA
-//     tensor reduce-adds (32 rows x D/2 columns per warp). A second kernel scales the workspace by
-//     sm_scale into the fp16 dQ.
-// TMEM: S^T [128] | dP^T [128] | P^T [64] | dV [D] | dK [D] | dQ_part [D].
+// diagonal block; causal tiles are taken longest first) over each (key tile, query block) pair, so S^T,
+// dP^T and the exponentials are computed once instead of once per output kernel (the reference's split,
+// kernels.py:151-321, recomputes QK^T and dO V^T for dQ). The persistent dK/dV structure (one CTA per
+// SM, 128-key tiles, static round-robin, ring of Q/dO blocks; K double-buffered because the dQ MMAs
+// read it to the end of a tile, V single-buffered and loaded by warp 11 once the tile's last dP^T MMA
+// has read it) plus:
+//   * -M and -delta are folded into the S^T and dP^T MMAs (one more K = 16 step each against a
+//     constant tile of ones), so the compute warps read S^T - M / qk_scale and dP^T - delta directly.
+//   * dS^T goes to shared memory ([128 keys, BQ queries] fp16, 128-byte swizzle, 64-query chunks).
+//     The same bytes are the K-major A operand of dK += dS^T Q and the MN-major operand of the dQ MMA
+//     (rows = keys, 128 contiguous bytes = 64 queries); at D = 128 dS^T also goes to TMEM as the A
+//     operand of the dK MMA.
+//   * dQ_part of a block (fp32; D <= 64: 128 queries x D, D = 128: transposed, D x 64 queries) is
+//     accumulated in TMEM by its own MMAs; the compute warps read it one block later, right after
+//     handing over the next block's P^T/dS^T (the dQ MMAs of that block wait for the read: dq_read),
+//     and add it into a dense fp32 workspace through TMA tensor reduce-adds (one 32 x 32 box per warp).
+//   * After its last tile every CTA (a cooperative launch of at most one CTA per SM) waits at a grid
+//     barrier for all reduce-adds, then its compute warps scale a share of the workspace by sm_scale
+//     into the fp16 dQ.
+// TMEM (D <= 64): S^T [128] | dP^T [128] | P^T [64] | dV [D] | dK [D] | dQ_part [D]; D = 128: FusedCfg.
 template <int D>
 struct FusedCfg {
   using G = Geo<D>;
