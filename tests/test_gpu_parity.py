@@ -358,14 +358,21 @@ def _torch_ref(q, k, v, do, causal, scale):
         ((4, 16, 4096, 64), False, [(0, 0), (1, 7), (2, 13), (3, 15)]),
         ((1, 16, 16384, 64), True, [(0, 0), (0, 5), (0, 15)]),
         ((64, 16, 8192, 64), True, [(0, 0), (21, 3), (42, 9), (63, 15)]),
+        # the other head dims at the config-2 length: D = 128 runs the fused backward's 64-query blocks
+        # and transposed dQ part, D = 16 / 32 its narrow swizzles
+        ((2, 8, 4096, 128), False, [(0, 0), (1, 7)]),
+        ((2, 8, 4096, 128), True, [(0, 3), (1, 5)]),
+        ((2, 8, 4096, 32), True, [(0, 0), (1, 7)]),
+        ((2, 8, 4096, 16), False, [(0, 2), (1, 6)]),
     ],
-    ids=["cfg2_b4h16n4096", "cfg3_b1h16n16384_causal", "cfg5_b64h16n8192_causal"],
+    ids=["cfg2_b4h16n4096", "cfg3_b1h16n16384_causal", "cfg5_b64h16n8192_causal", "b2h8n4096_d128",
+         "b2h8n4096_d128_causal", "b2h8n4096_d32_causal", "b2h8n4096_d16"],
 )
 def test_full_size_against_fp32_definition(shape, causal, heads) -> None:
     """BASELINE configs 2, 3 and 5 at full size (config 5 is the scaling config: 1,024 pairs, 1 GiB per
-    tensor); (batch, head) pairs from the first, middle and last parts of the batch checked against the
-    fp32 definition. Plain max-abs bound 2e-3 for O and dq/dk/dv (values are all well below 1 at these
-    lengths), 1e-3 for M."""
+    tensor), and head dims 128, 32 and 16 at the config-2 length; (batch, head) pairs from the first,
+    middle and last parts of the batch checked against the fp32 definition. Plain max-abs bound 2e-3 for
+    O and dq/dk/dv (values are all well below 1 at these lengths), 1e-3 for M."""
     b, h, n, d = shape
     g = torch.Generator(device="cuda").manual_seed(2024)
     q, k, v, do = (torch.randn(shape, generator=g, device="cuda").to(torch.float16) for _ in range(4))
