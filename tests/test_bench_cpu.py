@@ -1,5 +1,6 @@
-"""bench.py host logic that needs no GPU: the reference arm's JSON line, and the clock sampler that records SM clocks and throttle reasons
-during the timed region, driven here by a stand-in `nvidia-smi` on PATH."""
+"""bench.py host logic that needs no GPU: the reference arm's JSON line, and the clock sampler that
+records SM clocks and throttle reasons during the timed region, driven here by a stand-in `nvidia-smi`
+on PATH."""
 
 from __future__ import annotations
 
